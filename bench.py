@@ -1,0 +1,409 @@
+"""Benchmark of the sm_100a attention forward (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C2] [--impl ours|reference]
+
+A step is one attention forward over one batch of the workload. At N=1 the
+workload is C2 (B=1, H=24, Sq=Skv=4096, D=128, fp16; the configuration the
+north-star target is quoted on). Under torchrun with N ranks every rank runs
+its own C2-sized batch of (batch x head) units -- the path shards by
+(batch x head) with no data exchange -- so the scaling is weak and `value`
+is the whole-job TFLOP/s = N * flops / max-over-ranks time.
+
+Timing: W untimed warm-up steps, then K steps back to back between CUDA
+events on the launching stream, bracketed by a barrier and
+torch.cuda.synchronize() on both sides. Inputs rotate over enough distinct
+sets that their total is larger than the 126 MB L2, so no step reads inputs
+the previous step left in L2. SM clocks and throttle reasons are sampled
+through NVML while the timed steps run.
+
+`e2e` repeats the measurement through the public operator with the inputs in
+pinned host memory: each step copies q, k, v host->device, runs the operator
+and copies o back, all inside the timed region.
+
+`--impl reference` times the reference's CPU path (fp32 SDPA MATH on the host
+cores, from the CPU oracle) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+from gfx906_b200.configs import CONFIGS, AttnConfig, make_qkv  # noqa: E402
+
+METRIC = "attn fwd TFLOP/s (4*B*H*Sq*Skv*D)"
+UNIT = "TFLOP/s"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--config", default="C2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), float(d.get("hbm_gbs", 6650.0)), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def profiled_traffic(cfg_name: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    f = ROOT / "profiles" / f"attn_fwd_{cfg_name}_traffic.txt"
+    if not f.is_file():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML in a thread."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        "display_clocks_setting": 0x100,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.period = period_s
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            uuid = torch.cuda.get_device_properties(device_index).uuid
+            h = None
+            try:
+                h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + str(uuid)).encode())
+            except Exception:  # noqa: BLE001
+                h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self._h = h
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - no NVML: clocks stay unknown
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for name, bit in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        med = statistics.median(self.samples) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def rank_config(cfg: AttnConfig, rank: int) -> AttnConfig:
+    """Rank r's own batch of (batch x head) units: same shape, its own seed."""
+    return AttnConfig(cfg.name, cfg.B, cfg.H, cfg.Sq, cfg.Skv, cfg.D, cfg.seed + 1000 * rank, cfg.std)
+
+
+def cpu_baseline(cfg: AttnConfig, seconds: float):
+    """The reference's CPU path (fp32 SDPA MATH) on a bounded sample of cfg."""
+    from oracle.sdpa_math import sdpa_math_fp32
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    q, k, v = make_qkv(1, 1, min(cfg.Sq, 512), cfg.Skv, cfg.D, seed=cfg.seed, std=cfg.std)
+    sdpa_math_fp32(q, k, v, cfg.scale)  # warm-up
+    t0 = time.perf_counter()
+    sdpa_math_fp32(q, k, v, cfg.scale)
+    probe = time.perf_counter() - t0
+    rate_rows = q.shape[2] / max(probe, 1e-6)  # query rows per second (one head)
+    rows = int(min(cfg.Sq, max(64, rate_rows * seconds / 3)))
+    heads = max(1, min(cfg.B * cfg.H, int(rate_rows * seconds / max(rows, 1) / 1.0)))
+    heads = min(heads, cfg.B * cfg.H)
+    q, k, v = make_qkv(1, heads, rows, cfg.Skv, cfg.D, seed=cfg.seed, std=cfg.std)
+    t0 = time.perf_counter()
+    sdpa_math_fp32(q, k, v, cfg.scale)
+    dt = time.perf_counter() - t0
+    flops = 4.0 * heads * rows * cfg.Skv * cfg.D
+    return {
+        "value": flops / dt / 1e12,
+        "unit": UNIT,
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": (f"fp32 SDPA MATH on the host CPU over {heads} head(s) x {rows} query rows x "
+                   f"{cfg.Skv} keys x D={cfg.D} of {cfg.name} ({flops / 1e9:.1f} GFLOP, {dt:.2f} s)"),
+    }
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU path on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    from oracle.sdpa_math import sdpa_math_fp32
+
+    cfg = CONFIGS[args.config]
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    budget = 90.0  # seconds for all warm-up + timed steps together
+    q, k, v = make_qkv(1, 1, min(cfg.Sq, 256), cfg.Skv, cfg.D, seed=cfg.seed, std=cfg.std)
+    sdpa_math_fp32(q, k, v, cfg.scale)
+    t0 = time.perf_counter()
+    sdpa_math_fp32(q, k, v, cfg.scale)
+    rate_rows = q.shape[2] / max(time.perf_counter() - t0, 1e-6)
+    per_step = budget / max(1, args.steps + args.warmup)
+    rows = int(max(16, min(cfg.Sq, rate_rows * per_step)))
+    q, k, v = make_qkv(1, 1, rows, cfg.Skv, cfg.D, seed=cfg.seed, std=cfg.std)
+    for _ in range(args.warmup):
+        sdpa_math_fp32(q, k, v, cfg.scale)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        sdpa_math_fp32(q, k, v, cfg.scale)
+    dt = time.perf_counter() - t0
+    flops = 4.0 * rows * cfg.Skv * cfg.D * args.steps
+    value = flops / dt / 1e12
+    sample = (f"each step: fp32 SDPA MATH over 1 head x {rows} query rows x {cfg.Skv} keys x "
+              f"D={cfg.D} of {cfg.name} (host CPU, {torch.get_num_threads()} threads)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"{cfg.name}: {cfg.describe()}", "sample_rows": rows},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local):
+    import gfx906_b200
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    mod = gfx906_b200.load_attention()
+    if mod is None:
+        raise RuntimeError(f"sm_100 attention operator unavailable: {gfx906_b200.last_error()}")
+    base = CONFIGS[args.config]
+    cfg = rank_config(base, rank)
+    scale = cfg.scale
+
+    # distinct input sets so that the rotation exceeds L2
+    set_bytes = cfg.io_bytes
+    nsets = max(2, math.ceil(2 * L2_BYTES / set_bytes) + 1)
+    nsets = min(nsets, 8)
+    q0, k0, v0 = make_qkv(cfg.B, cfg.H, cfg.Sq, cfg.Skv, cfg.D, cfg.seed, cfg.std)
+    sets = []
+    for i in range(nsets):
+        # same values, distinct buffers (the kernel's time does not depend on values)
+        sets.append((q0.to(dev), k0.to(dev), v0.to(dev)))
+    outs = [torch.empty_like(s[0]) for s in sets]
+    lib_launch = _c_launcher()
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        q, k, v = sets[i % nsets]
+        o = outs[i % nsets]
+        rc = lib_launch(q, k, v, o, cfg, scale, stream)
+        if rc != 0:
+            raise RuntimeError(f"launch failed with status {rc}")
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with sampler:
+        start.record(stream)
+        for i in range(args.steps):
+            step(i)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = start.elapsed_time(end)
+    ms_max = max_over_ranks(ms, world)
+    if mod.device_status(False) != 0:
+        raise RuntimeError("a kernel wait timed out during the benchmark")
+
+    flops_step = cfg.flops
+    value = world * flops_step * args.steps / (ms_max * 1e-3) / 1e12
+    per_launch_ms = ms / args.steps
+    achieved = flops_step / (per_launch_ms * 1e-3) / 1e12
+
+    # ---- e2e through the public operator, host buffers, copies in the timed region
+    hq = q0.pin_memory()
+    hk = k0.pin_memory()
+    hv = v0.pin_memory()
+    hout = torch.empty(hq.shape, dtype=hq.dtype, pin_memory=True)
+    e2e_steps = max(1, args.e2e_steps)
+
+    def e2e_step():
+        dq = hq.to(dev, non_blocking=True)
+        dk = hk.to(dev, non_blocking=True)
+        dv = hv.to(dev, non_blocking=True)
+        o = gfx906_b200.attn(dq, dk, dv, scale)
+        hout.copy_(o, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_value = world * flops_step * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    h2d = (hq.numel() + hk.numel() + hv.numel()) * hq.element_size()
+    d2h = hout.numel() * hout.element_size()
+
+    if rank != 0:
+        return
+    peak_tf, _, peak_kind = load_peaks()
+    traffic = profiled_traffic(base.name)
+    clocks = sampler.summary()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic",
+        "config": {
+            "workload": f"{base.name}: {base.describe()}",
+            "per_rank": f"each rank its own B*H={cfg.B * cfg.H} heads (weak scaling over (batch x head))",
+            "l2": f"inputs rotate over {nsets} distinct sets ({nsets * set_bytes / 2**20:.0f} MiB > 126 MB L2)",
+            "parallelism": f"shard (batch x head) over {world} GPU(s), no collective on the data path",
+        },
+        "roofline": {
+            "bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": UNIT,
+            "frac": achieved / peak_tf,
+            "peak_source": f"{peak_kind} bf16 dense burst (MEASURED_PEAKS.json bf16_tflops)",
+            "traffic": traffic,
+            "algorithmic_bytes": cfg.io_bytes,
+            "kernel": f"attn_fwd_kernel<{128 if cfg.D == 128 else 64}>" if cfg.D <= 128 else "attn_fwd_d512",
+        },
+        "clocks": clocks,
+        "gpu_launches": args.steps * _launches_per_call(cfg),
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "ms_per_step": e2e_ms / e2e_steps},
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(base, args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+
+
+def _launches_per_call(cfg: AttnConfig) -> int:
+    return 1
+
+
+def _c_launcher():
+    """Direct C-ABI launch on preallocated outputs (no allocation in the timed loop)."""
+    from gfx906_b200 import build
+    from gfx906_b200.cabi import CABI
+
+    lib = CABI(build.LIB_PATH)
+
+    def launch(q, k, v, o, cfg, scale, stream):
+        return lib.launch_status(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), cfg.B,
+                                 cfg.H, cfg.Sq, cfg.Skv, cfg.D, scale, stream.cuda_stream)
+
+    return launch
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_env()
+    if world > 1:
+        import datetime
+
+        if args.impl == "reference":
+            # only rank 0 works; the other ranks exit without joining anything
+            run_reference(args, rank, world)
+            return
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world, local)
+    finally:
+        if world > 1 and torch.distributed.is_initialized():
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,32 @@
+"""B200 (sm_100a) flash-attention forward with the gfx906 extension's surface.
+
+Public entry points:
+
+* ``attn(q, k, v, scale)``: the operator itself (fp16 [B,H,S,D] CUDA tensors).
+  Raises if the native operator cannot be loaded; there is no fallback.
+* ``load_attention()`` / ``is_sm100()``: the lazy loader, as in the
+  reference's ``deploy/gfx906_attn.py`` (returns None instead of raising).
+* ``gfx906_attention.install()``: the ComfyUI hook with eligibility gating and
+  stock fallback, as in the reference's ``deploy/gfx906_attention.py``.
+"""
+
+from .gfx906_attn import is_sm100, last_error, load_attention
+
+__all__ = ["attn", "device_status", "is_sm100", "load_attention", "last_error"]
+
+
+def _module_or_raise():
+    mod = load_attention()
+    if mod is None:
+        raise RuntimeError(f"gfx906_b200: sm_100 attention operator unavailable: {last_error()}")
+    return mod
+
+
+def attn(q, k, v, scale):
+    """O = softmax(scale * q @ k^T) @ v on the sm_100a kernel (fp16 [B,H,S,D])."""
+    return _module_or_raise().attn(q, k, v, scale)
+
+
+def device_status(reset: bool = False) -> int:
+    """0 unless a kernel wait timed out since the last reset (synchronises)."""
+    return _module_or_raise().device_status(reset)

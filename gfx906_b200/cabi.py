@@ -1,0 +1,52 @@
+"""ctypes binding of the C-ABI library (``include/gfx906_b200_attn.h``).
+
+This is the stub a host application without torch would write to call the
+library; the tests use it to check the exported surface and to drive the
+C-ABI directly with device pointers.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+STATUS = {"OK": 0, "EINVAL": 1, "EHEADDIM": 2, "EALIGN": 3, "ENODEV": 4, "ECUDA": 5, "ETIMEOUT": 6}
+
+_c_int, _c_void_p, _c_float = ctypes.c_int, ctypes.c_void_p, ctypes.c_float
+
+
+class CABI:
+    """Loaded ``libgfx906_b200_attn.so`` with typed entry points."""
+
+    def __init__(self, path):
+        self.path = Path(path)
+        self.dll = ctypes.CDLL(str(self.path))
+        d = self.dll
+        sig = [_c_void_p] * 4 + [_c_int] * 5 + [_c_float, _c_void_p]
+        d.launch.argtypes, d.launch.restype = sig, None
+        d.gfx906_b200_attn_launch.argtypes, d.gfx906_b200_attn_launch.restype = sig, _c_int
+        d.gfx906_b200_attn_last_error.argtypes, d.gfx906_b200_attn_last_error.restype = [], _c_int
+        d.gfx906_b200_attn_error_string.argtypes = [_c_int]
+        d.gfx906_b200_attn_error_string.restype = ctypes.c_char_p
+        d.gfx906_b200_attn_device_status.argtypes = [_c_int]
+        d.gfx906_b200_attn_device_status.restype = _c_int
+        d.gfx906_b200_attn_timeout_info.argtypes = [ctypes.POINTER(_c_int)]
+        d.gfx906_b200_attn_timeout_info.restype = _c_int
+        d.gfx906_b200_attn_selftest_wait_timeout.argtypes = [ctypes.c_ulonglong, _c_void_p]
+        d.gfx906_b200_attn_selftest_wait_timeout.restype = _c_int
+        d.gfx906_b200_attn_flops.argtypes = [_c_int] * 5
+        d.gfx906_b200_attn_flops.restype = ctypes.c_double
+
+    def launch_status(self, q, k, v, o, B, H, Sq, Skv, D, scale, stream=None) -> int:
+        return self.dll.gfx906_b200_attn_launch(q, k, v, o, B, H, Sq, Skv, D, _c_float(scale), stream)
+
+    def error_string(self, status: int) -> str:
+        return self.dll.gfx906_b200_attn_error_string(status).decode()
+
+    def device_status(self, reset: bool = False) -> int:
+        return self.dll.gfx906_b200_attn_device_status(1 if reset else 0)
+
+    def timeout_info(self):
+        buf = (_c_int * 6)()
+        rc = self.dll.gfx906_b200_attn_timeout_info(buf)
+        return rc, list(buf)

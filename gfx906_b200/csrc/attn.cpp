@@ -1,0 +1,50 @@
+// Torch operator `attn(q, k, v, scale) -> o` over the C-ABI launch shim.
+//
+// Same Python name, signature and checks as the reference binding
+// (attn.cpp:6-21): q must be a CUDA fp16 tensor, k and v must have equal
+// shapes, batch / heads / head_dim must match q, head_dim must be <= 64 and a
+// multiple of 8, or 128, or 512; inputs are made contiguous, the output is a
+// new contiguous [B,H,Sq,D] fp16 tensor, and the kernel is launched on the
+// current stream of q's device. Two checks are added: k and v must also be
+// CUDA fp16 tensors on q's device (the reference only checked q), and every
+// tensor must be 4-D. Failures raise RuntimeError (TORCH_CHECK).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "../../include/gfx906_b200_attn.h"
+
+torch::Tensor attn(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale) {
+  TORCH_CHECK(q.is_cuda() && q.dtype() == torch::kHalf, "kernel: q must be a CUDA float16 tensor");
+  TORCH_CHECK(k.is_cuda() && v.is_cuda() && k.dtype() == torch::kHalf && v.dtype() == torch::kHalf,
+              "kernel: k and v must be CUDA float16 tensors");
+  TORCH_CHECK(k.device() == q.device() && v.device() == q.device(),
+              "kernel: q, k and v must be on the same device");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "kernel: q/k/v must be [B,H,S,D]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(k.sizes() == v.sizes() && q.size(0) == k.size(0) && q.size(1) == k.size(1) &&
+                  q.size(3) == k.size(3),
+              "kernel: q/k/v shape mismatch");
+  const auto B = q.size(0), H = q.size(1), Sq = q.size(2), Skv = k.size(2), D = q.size(3);
+  TORCH_CHECK((D <= 64 && D % 8 == 0) || D == 128 || D == 512,
+              "kernel: head_dim<=64 multiple of 8, 128, or 512");
+  TORCH_CHECK(B <= INT32_MAX && H <= INT32_MAX && Sq <= INT32_MAX && Skv <= INT32_MAX,
+              "kernel: sizes must fit in int32");
+  auto qc = q.contiguous(), kc = k.contiguous(), vc = v.contiguous();
+  auto o = torch::empty_like(qc);
+  const int rc = gfx906_b200_attn_launch(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(),
+                                         static_cast<int>(B), static_cast<int>(H), static_cast<int>(Sq),
+                                         static_cast<int>(Skv), static_cast<int>(D),
+                                         static_cast<float>(scale), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == GFX906_B200_OK, "kernel: ", gfx906_b200_attn_error_string(rc));
+  return o;
+}
+
+// Device status word of the current device (see gfx906_b200_attn_device_status).
+// Returns 0 when no kernel wait has timed out. Synchronises.
+int64_t device_status(bool reset) { return gfx906_b200_attn_device_status(reset ? 1 : 0); }
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("attn", &attn, "flash-attention forward (fp16 [B,H,S,D], sm_100a)");
+  m.def("device_status", &device_status, "device status word (0 = ok)", pybind11::arg("reset") = false);
+}

@@ -1,0 +1,703 @@
+// Flash-attention forward for NVIDIA B200 (sm_100a).
+//
+// Computes O = softmax(scale * Q K^T) V for fp16 [B,H,S,D] tensors, the
+// operation of the reference's HIP kernels (attn_kernel.hip:146-708) behind its
+// C-ABI `launch` (attn_kernel.hip:710-742). The algorithm is the same tiled
+// online softmax: K/V are streamed in key tiles, each query row keeps a running
+// max m and running sum l, partial outputs are rescaled by exp(m_old - m_new)
+// when the max grows (attn_kernel.hip:452-462, 491-492), and the output is
+// O / l at the end (attn_kernel.hip:497-511). The S x S score matrix is never
+// written to memory.
+//
+// The B200 design:
+//  * One CTA owns two 128-row query tiles of one (batch, head). Both are
+//    multiplied against every 128-key K/V tile, so each K/V tile is read from
+//    L2 once per 256 query rows.
+//  * A producer warp streams Q (once) and K/V tiles (in a ring of shared-memory
+//    stages) with TMA, 128-byte swizzled, completion tracked by mbarriers.
+//  * One thread of the MMA warp issues every tcgen05.mma: S_i = Q_i K^T
+//    (fp16 x fp16 -> fp32, both operands from shared memory) into tensor memory
+//    (TMEM), and O_i += P_i V with P_i read from TMEM and V from shared memory.
+//  * Two softmax warpgroups (one per query tile, one thread per query row =
+//    one TMEM lane) read S_i from TMEM, update m and l in fp32, write
+//    P_i = exp2(S_i * scale * log2(e) - m) as fp16 back into the S_i columns of
+//    TMEM, and rescale their O_i rows in TMEM when the max grows by more than
+//    2^8 (otherwise the stale max is kept: O and l carry the same factor, so
+//    O / l is unchanged, and P stays <= 256).
+//  * The MMA order S0(j), PV1(j-1), S1(j), PV0(j) lets softmax 0 run while the
+//    tensor core works on tile 1 and vice versa.
+//  * Epilogue: O_i / l -> fp16 -> swizzled shared memory (reusing Q_i's
+//    buffer) -> TMA store, which clips rows beyond Sq.
+//
+// TMEM columns (512 allocated): S0 [0,128), S1 [128,256), O0 [256,256+DP),
+// O1 [256+DP, 256+2*DP). P_i occupies the first 64 columns of S_i.
+//
+// Every mbarrier wait is bounded (time limit from the host). A wait that runs
+// out sets a CTA-wide abort flag and the device status word, the other roles
+// stop at their next wait, in-flight copies and MMAs are drained with bounded
+// waits, TMEM is freed and the kernel returns.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "../../include/gfx906_b200_attn.h"
+#include "sm100_ptx.cuh"
+
+namespace fa {
+
+constexpr int BM = 128;            // query rows per tile (= TMEM lanes)
+constexpr int BN = 128;            // keys per K/V tile
+constexpr int CHUNK_BYTES = 16384; // one 128-row x 64-col fp16 swizzled box
+constexpr int NUM_THREADS = 320;   // 8 softmax warps + producer + MMA
+constexpr int PRODUCER_WARP = 8;
+constexpr int MMA_WARP = 9;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+
+// Roles recorded in the timeout diagnostics.
+enum Role : int { ROLE_PRODUCER = 1, ROLE_MMA = 2, ROLE_SOFTMAX0 = 3, ROLE_SOFTMAX1 = 4 };
+
+// Device status word: bit 0 = a bounded wait ran out. Sticky until the host
+// clears it through gfx906_b200_attn_device_status(1).
+__device__ unsigned int g_status = 0;
+__device__ int g_timeout_info[6];
+
+struct Params {
+  int Sq;
+  int Skv;
+  int D;            // true head dim (<= DP)
+  int bh_offset;    // added to blockIdx.y
+  float scale_log2; // scale * log2(e)
+  unsigned long long timeout_ns;
+};
+
+template <int DP>
+struct Cfg {
+  static constexpr int NCHUNK = DP / 64;
+  static constexpr int TILE_BYTES = NCHUNK * CHUNK_BYTES;
+  static constexpr int STAGES = (DP == 128) ? 4 : 8;
+  static constexpr int NUM_BARS = 1 + 2 * STAGES + 2 + 2 + 2 + 1 + 2;
+  static constexpr int DATA_BYTES = (2 + STAGES) * TILE_BYTES;
+  static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + DATA_BYTES + NUM_BARS * 8 + 16;
+  // barrier indices
+  static constexpr int B_Q = 0;
+  static constexpr int B_KV_FULL = 1;
+  static constexpr int B_KV_EMPTY = 1 + STAGES;
+  static constexpr int B_S_FULL = 1 + 2 * STAGES;
+  static constexpr int B_P_FULL = B_S_FULL + 2;
+  static constexpr int B_O_FULL = B_P_FULL + 2;
+  static constexpr int B_DRAIN = B_O_FULL + 2;
+  static constexpr int B_EPI = B_DRAIN + 1;  // 2 barriers: staging written, per tile
+};
+
+__device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                       unsigned long long timeout_ns, int bar_idx, int role) {
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t n = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if ((++n & 31u) == 0u) {
+      const uint64_t t = globaltimer_ns();
+      if (t - t0 > timeout_ns || n > (1u << 24)) {
+        *abort_flag = 1;
+        if (atomicCAS(&g_status, 0u, 1u) == 0u) {
+          g_timeout_info[0] = blockIdx.x;
+          g_timeout_info[1] = blockIdx.y;
+          g_timeout_info[2] = threadIdx.x / 32;
+          g_timeout_info[3] = bar_idx;
+          g_timeout_info[4] = static_cast<int>(parity);
+          g_timeout_info[5] = role;
+          __threadfence();
+        } else {
+          atomicOr(&g_status, 1u);
+        }
+        return false;
+      }
+    }
+  }
+}
+
+// Bounded wait for completion of the phase with the given parity.
+__device__ __forceinline__ bool bwait(uint32_t bars, int idx, uint32_t parity,
+                                      volatile int* abort_flag, unsigned long long timeout_ns,
+                                      int role) {
+  const uint32_t bar = bars + 8u * idx;
+  if (mbar_try_wait(bar, parity)) return true;
+  return wait_slow(bar, parity, abort_flag, timeout_ns, idx, role);
+}
+
+// Warp-uniform bounded wait: every lane gets the same answer, so the
+// warp-collective tcgen05.ld/st that follow are never reached by part of a warp.
+__device__ __forceinline__ bool bwait_warp(uint32_t bars, int idx, uint32_t parity,
+                                           volatile int* abort_flag, unsigned long long timeout_ns,
+                                           int role) {
+  const bool ok = bwait(bars, idx, parity, abort_flag, timeout_ns, role);
+  return __all_sync(0xffffffffu, ok);
+}
+
+template <int DP>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                    const Params p) {
+  using C = Cfg<DP>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t s0 = (raw + 1023u) & ~1023u;  // 1024-B aligned for the 128B swizzle
+  uint8_t* smem = smem_raw + (s0 - raw);
+  const uint32_t sQ0 = s0;
+  const uint32_t sQ1 = s0 + C::TILE_BYTES;
+  const uint32_t sKV = s0 + 2 * C::TILE_BYTES;
+  const uint32_t bars = s0 + C::DATA_BYTES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::DATA_BYTES + C::NUM_BARS * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* drain_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);  // stays 0
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int bh = blockIdx.y + p.bh_offset;
+  const int q_row0 = blockIdx.x * (2 * BM);
+  const int n_tiles = (p.Skv + BN - 1) / BN;
+  const bool has1 = (q_row0 + BM) < p.Sq;  // second query tile has live rows
+
+  if (threadIdx.x == 0) {
+    mbar_init(bars + 8 * C::B_Q, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(bars + 8 * (C::B_KV_FULL + s), 1);
+      mbar_init(bars + 8 * (C::B_KV_EMPTY + s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bars + 8 * (C::B_S_FULL + i), 1);
+      mbar_init(bars + 8 * (C::B_P_FULL + i), BM);
+      mbar_init(bars + 8 * (C::B_O_FULL + i), 1);
+      mbar_init(bars + 8 * (C::B_EPI + i), BM);
+    }
+    mbar_init(bars + 8 * C::B_DRAIN, 1);
+    *abort_flag = 0;
+    *drain_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const unsigned long long tmo = p.timeout_ns;
+
+  if (warp == PRODUCER_WARP) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_o);
+      mbar_arrive_expect_tx(bars + 8 * C::B_Q, (has1 ? 2 : 1) * C::TILE_BYTES);
+#pragma unroll
+      for (int c = 0; c < C::NCHUNK; ++c) {
+        tma_load_3d(sQ0 + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q, c * 64, q_row0, bh);
+        if (has1)
+          tma_load_3d(sQ1 + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q, c * 64, q_row0 + BM, bh);
+      }
+      int it = 0;
+      bool ok = true;
+      for (int j = 0; j < n_tiles && ok; ++j) {
+#pragma unroll
+        for (int kv = 0; kv < 2; ++kv) {
+          const int slot = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!bwait(bars, C::B_KV_EMPTY + slot, ph ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full = bars + 8 * (C::B_KV_FULL + slot);
+          mbar_arrive_expect_tx(full, C::TILE_BYTES);
+          const CUtensorMap* m = kv ? &tm_v : &tm_k;
+#pragma unroll
+          for (int c = 0; c < C::NCHUNK; ++c)
+            tma_load_3d(sKV + slot * C::TILE_BYTES + c * CHUNK_BYTES, m, full, c * 64, j * BN, bh);
+          ++it;
+        }
+      }
+      if (!ok) {
+        // Drain: every load issued must land before the CTA's shared memory goes away.
+        if (!mbar_try_wait(bars + 8 * C::B_Q, 0))
+          wait_slow(bars + 8 * C::B_Q, 0, drain_flag, 100000000ull, C::B_Q, ROLE_PRODUCER);
+        const int first = it > C::STAGES ? it - C::STAGES : 0;
+        for (int t = first; t < it; ++t) {
+          const int slot = t % C::STAGES;
+          const uint32_t ph = (t / C::STAGES) & 1;
+          if (!mbar_try_wait(bars + 8 * (C::B_KV_FULL + slot), ph))
+            wait_slow(bars + 8 * (C::B_KV_FULL + slot), ph, drain_flag, 100000000ull,
+                      C::B_KV_FULL + slot, ROLE_PRODUCER);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == MMA_WARP) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC_QK = idesc_f16_f32(BM, BN, 0, 0);
+      const int dpv = (p.D + 15) & ~15;  // PV N dimension (multiple of 16)
+      const uint32_t idesc_pv = idesc_f16_f32(BM, dpv, 0, 1);
+      const int ksteps = (p.D + 15) / 16;  // QK reduction steps over the head dim
+      const uint32_t tS0 = tmem + 0, tS1 = tmem + 128;
+      const uint32_t tO0 = tmem + 256, tO1 = tmem + 256 + DP;
+
+      auto issue_qk = [&](uint32_t d_tmem, uint32_t sQ, uint32_t sK) {
+        for (int k = 0; k < ksteps; ++k) {
+          const uint32_t off = (k >> 2) * CHUNK_BYTES + (k & 3) * 32;
+          mma_f16_ss(d_tmem, sdesc_sw128(sQ + off, 16, 1024), sdesc_sw128(sK + off, 16, 1024),
+                     IDESC_QK, k > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](uint32_t d_tmem, uint32_t p_tmem, uint32_t sV, bool acc) {
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k) {
+          mma_f16_ts(d_tmem, p_tmem + 8 * k, sdesc_sw128(sV + k * 2048, CHUNK_BYTES, 1024), idesc_pv,
+                     (acc || k > 0) ? 1u : 0u);
+        }
+      };
+
+      bool ok = bwait(bars, C::B_Q, 0, abort_flag, tmo, ROLE_MMA);
+      tc_fence_after();
+      int it = 0;
+      int prev_v_slot = 0;
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int k_slot = it % C::STAGES;
+        const uint32_t k_ph = (it / C::STAGES) & 1;
+        ++it;
+        const int v_slot = it % C::STAGES;
+        const uint32_t v_ph = (it / C::STAGES) & 1;
+        ++it;
+        const uint32_t sK = sKV + k_slot * C::TILE_BYTES;
+        const uint32_t sV = sKV + v_slot * C::TILE_BYTES;
+
+        if (!bwait(bars, C::B_KV_FULL + k_slot, k_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+        tc_fence_after();
+        issue_qk(tS0, sQ0, sK);  // S0(j); PV0(j-1) was issued before it
+        tc_commit(bars + 8 * (C::B_S_FULL + 0));
+        if (has1) {
+          if (j > 0) {
+            if (!bwait(bars, C::B_P_FULL + 1, (j - 1) & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(tO1, tS1, sKV + prev_v_slot * C::TILE_BYTES, j - 1 > 0);
+            tc_commit(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));  // V(j-1) free
+          }
+          issue_qk(tS1, sQ1, sK);
+          tc_commit(bars + 8 * (C::B_S_FULL + 1));
+        }
+        tc_commit(bars + 8 * (C::B_KV_EMPTY + k_slot));  // K(j) free
+        if (!bwait(bars, C::B_KV_FULL + v_slot, v_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+        if (!bwait(bars, C::B_P_FULL + 0, j & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(tO0, tS0, sV, j > 0);
+        if (!has1) tc_commit(bars + 8 * (C::B_KV_EMPTY + v_slot));
+        prev_v_slot = v_slot;
+      }
+      if (ok && has1 && n_tiles > 0) {
+        if (bwait(bars, C::B_P_FULL + 1, (n_tiles - 1) & 1, abort_flag, tmo, ROLE_MMA)) {
+          tc_fence_after();
+          issue_pv(tO1, tS1, sKV + prev_v_slot * C::TILE_BYTES, n_tiles - 1 > 0);
+          tc_commit(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));
+        } else {
+          ok = false;
+        }
+      }
+      if (ok) {
+        tc_commit(bars + 8 * (C::B_O_FULL + 0));
+        if (has1) tc_commit(bars + 8 * (C::B_O_FULL + 1));
+      } else {
+        // Drain every MMA issued so far before TMEM and shared memory are released.
+        tc_commit(bars + 8 * C::B_DRAIN);
+        wait_slow(bars + 8 * C::B_DRAIN, 0, drain_flag, 100000000ull, C::B_DRAIN, ROLE_MMA);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int ti = warp >> 2;  // query tile
+    const int quad = warp & 3; // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    const int role = ti ? ROLE_SOFTMAX1 : ROLE_SOFTMAX0;
+    if (ti == 0 || has1) {
+      const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+      const uint32_t tS = tmem + lane_off + ti * 128;
+      const uint32_t tO = tmem + lane_off + 256 + ti * DP;
+      const float sl2 = p.scale_log2;
+      const bool pos = sl2 >= 0.f;
+      float m_run = -INFINITY;  // running max, already multiplied by scale*log2(e)
+      float l_run = 0.f;
+      bool ok = true;
+      for (int j = 0; j < n_tiles; ++j) {
+        if (!bwait_warp(bars, C::B_S_FULL + ti, j & 1, abort_flag, tmo, role)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t s[BN];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + 32 * c, s + 32 * c);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) reg_fence32(s + 32 * c);
+
+        const int nvalid = min(BN, p.Skv - j * BN);
+        const bool full = nvalid == BN;
+        // Row extreme of the raw scores: max for scale >= 0, min for scale < 0,
+        // so that extreme * scale is the max of the scaled scores.
+        float mx;
+        {
+          float a0 = pos ? -INFINITY : INFINITY, a1 = a0, a2 = a0, a3 = a0;
+          if (full) {
+            if (pos) {
+#pragma unroll
+              for (int c = 0; c < BN; c += 4) {
+                a0 = fmaxf(a0, __uint_as_float(s[c]));
+                a1 = fmaxf(a1, __uint_as_float(s[c + 1]));
+                a2 = fmaxf(a2, __uint_as_float(s[c + 2]));
+                a3 = fmaxf(a3, __uint_as_float(s[c + 3]));
+              }
+              mx = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
+            } else {
+#pragma unroll
+              for (int c = 0; c < BN; c += 4) {
+                a0 = fminf(a0, __uint_as_float(s[c]));
+                a1 = fminf(a1, __uint_as_float(s[c + 1]));
+                a2 = fminf(a2, __uint_as_float(s[c + 2]));
+                a3 = fminf(a3, __uint_as_float(s[c + 3]));
+              }
+              mx = fminf(fminf(a0, a1), fminf(a2, a3));
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN; ++c) {
+              const float x = __uint_as_float(s[c]);
+              if (c < nvalid) a0 = pos ? fmaxf(a0, x) : fminf(a0, x);
+            }
+            mx = a0;
+          }
+        }
+        const float m_cand = mx * sl2;
+        const float m_new = fmaxf(m_run, m_cand);
+        const bool need = m_new > m_run + RESCALE_THRESHOLD;
+        float factor = 1.f;
+        if (need) {
+          factor = ex2_approx(m_run - m_new);  // 0 on the first tile (m_run = -inf)
+          m_run = m_new;
+        }
+        l_run *= factor;
+        const float neg_m = -m_run;
+        // P = exp2(s * scale*log2(e) - m) as fp16 into the first 64 columns of
+        // S, written in two halves so that half of s[] is dead before the rest.
+        float lsum0 = 0.f, lsum1 = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int c2 = 0; c2 < 32; ++c2) {
+            const int c = h * 64 + 2 * c2;
+            float e0 = ex2_approx(fmaf(__uint_as_float(s[c]), sl2, neg_m));
+            float e1 = ex2_approx(fmaf(__uint_as_float(s[c + 1]), sl2, neg_m));
+            if (!full) {
+              e0 = (c < nvalid) ? e0 : 0.f;
+              e1 = (c + 1 < nvalid) ? e1 : 0.f;
+            }
+            lsum0 += e0;
+            lsum1 += e1;
+            pk[c2] = pack_half2(e0, e1);
+          }
+          tmem_st32(tS + 32 * h, pk);
+        }
+        l_run += lsum0 + lsum1;
+        // Rescale this warp's O rows when any of them moved its max. PV(j-1)
+        // of this tile completed before S(j) was signalled, and PV(j) is only
+        // issued after this warpgroup arrives on P_FULL below.
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll
+          for (int c = 0; c < DP / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + 32 * c, o);
+            tmem_wait_ld();
+            reg_fence32(o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+            tmem_st32(tO + 32 * c, o);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bars + 8 * (C::B_P_FULL + ti));
+      }
+      // ---------------------------------------------------------- epilogue
+      const bool have_o =
+          ok && n_tiles > 0 && bwait_warp(bars, C::B_O_FULL + ti, 0, abort_flag, tmo, role);
+      const uint32_t stage = ti ? sQ1 : sQ0;  // Q_i is dead: its last MMA completed
+      if (have_o) {
+        tc_fence_after();
+        const float inv = 1.f / l_run;
+#pragma unroll
+        for (int c = 0; c < C::NCHUNK; ++c) {
+          uint32_t o[64];
+          tmem_ld32(tO + 64 * c, o);
+          tmem_ld32(tO + 64 * c + 32, o + 32);
+          tmem_wait_ld();
+          reg_fence32(o);
+          reg_fence32(o + 32);
+          const uint32_t rowbase = stage + c * CHUNK_BYTES + row * 128;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint32_t a = pack_half2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
+            const uint32_t b = pack_half2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
+            const uint32_t cc = pack_half2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
+            const uint32_t d = pack_half2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
+            st_shared_v4(rowbase + ((u ^ (row & 7)) << 4), a, b, cc, d);
+          }
+        }
+        fence_proxy_async_smem();
+      }
+      // Every thread of the warpgroup arrives (written or not); one thread
+      // waits, bounded, for all 128 rows before storing the tile.
+      mbar_arrive(bars + 8 * (C::B_EPI + ti));
+      if (quad == 0 && lane == 0 && have_o &&
+          bwait(bars, C::B_EPI + ti, 0, abort_flag, tmo, role)) {
+#pragma unroll
+        for (int c = 0; c < C::NCHUNK; ++c)
+          tma_store_3d(&tm_o, stage + c * CHUNK_BYTES, c * 64, q_row0 + ti * BM, bh);
+        tma_store_commit();
+        tma_store_wait_read0();
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Self-test kernel: one thread waits on an mbarrier nothing arrives at.
+__global__ void wait_timeout_selftest_kernel(unsigned long long timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    bwait(smem_u32(&bar), 0, 0, &abort_flag, timeout_ns, 0);
+    // Complete the barrier's phase so nothing is left pending at exit.
+    mbar_arrive(smem_u32(&bar));
+  }
+  __syncthreads();
+}
+
+}  // namespace fa
+
+// ======================================================================= host
+
+namespace {
+
+thread_local int t_last_error = GFX906_B200_OK;
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// [B*H, S, D] fp16 tensor, boxes of 64 head-dim columns x `box_rows` rows, 128B swizzle.
+bool make_map(CUtensorMap* m, const void* base, int D, int S, long long BH, int box_rows) {
+  auto enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t gdim[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S),
+                        static_cast<cuuint64_t>(BH)};
+  cuuint64_t gstride[2] = {static_cast<cuuint64_t>(D) * 2,
+                           static_cast<cuuint64_t>(S) * static_cast<cuuint64_t>(D) * 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), gdim, gstride, box,
+                   estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+struct DeviceInfo {
+  bool checked = false;
+  bool sm100 = false;
+  bool attrs_set = false;
+};
+constexpr int kMaxDevices = 64;
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int check_device(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GFX906_B200_ECUDA;
+  if (dev < 0 || dev >= kMaxDevices) return GFX906_B200_ENODEV;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& di = g_dev[dev];
+  if (!di.checked) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+      return GFX906_B200_ECUDA;
+    di.sm100 = (major == 10 && minor == 0);
+    di.checked = true;
+  }
+  if (!di.sm100) return GFX906_B200_ENODEV;
+  if (!di.attrs_set) {
+    if (cudaFuncSetAttribute(fa::attn_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             fa::Cfg<64>::SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(fa::attn_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             fa::Cfg<128>::SMEM_BYTES) != cudaSuccess)
+      return GFX906_B200_ECUDA;
+    di.attrs_set = true;
+  }
+  *dev_out = dev;
+  return GFX906_B200_OK;
+}
+
+unsigned long long timeout_ns_from_env() {
+  static unsigned long long v = [] {
+    const char* e = getenv("GFX906_B200_WAIT_TIMEOUT_MS");
+    unsigned long long ms = e ? strtoull(e, nullptr, 10) : 0ull;
+    if (ms == 0ull) ms = 2000ull;
+    return ms * 1000000ull;
+  }();
+  return v;
+}
+
+template <int DP>
+int launch_dp(const void* q, const void* k, const void* v, void* o, long long BH, int Sq, int Skv,
+              int D, float scale, cudaStream_t stream) {
+  CUtensorMap mq, mk, mv, mo;
+  if (!make_map(&mq, q, D, Sq, BH, fa::BM) || !make_map(&mk, k, D, Skv, BH, fa::BN) ||
+      !make_map(&mv, v, D, Skv, BH, fa::BN) || !make_map(&mo, o, D, Sq, BH, fa::BM))
+    return GFX906_B200_ECUDA;
+  fa::Params prm;
+  prm.Sq = Sq;
+  prm.Skv = Skv;
+  prm.D = D;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.timeout_ns = timeout_ns_from_env();
+  const unsigned qblocks = static_cast<unsigned>((Sq + 2 * fa::BM - 1) / (2 * fa::BM));
+  for (long long off = 0; off < BH; off += 65535) {
+    const long long n = (BH - off) < 65535 ? (BH - off) : 65535;
+    prm.bh_offset = static_cast<int>(off);
+    dim3 grid(qblocks, static_cast<unsigned>(n), 1);
+    fa::attn_fwd_kernel<DP><<<grid, fa::NUM_THREADS, fa::Cfg<DP>::SMEM_BYTES, stream>>>(mq, mk, mv, mo, prm);
+    if (cudaGetLastError() != cudaSuccess) return GFX906_B200_ECUDA;
+  }
+  return GFX906_B200_OK;
+}
+
+int attn_launch_impl(const void* q, const void* k, const void* v, void* o, int B, int H, int Sq, int Skv,
+                     int D, float scale, cudaStream_t stream) {
+  if (B < 0 || H < 0 || Sq < 0 || Skv < 0) return GFX906_B200_EINVAL;
+  if (!((D >= 8 && D <= 64 && D % 8 == 0) || D == 128 || D == 512)) return GFX906_B200_EHEADDIM;
+  const long long BH = static_cast<long long>(B) * H;
+  if (BH == 0 || Sq == 0) return GFX906_B200_OK;
+  if (BH > (1ll << 31) || static_cast<long long>(Sq) * D * 2 * BH >= (1ll << 40) ||
+      static_cast<long long>(Skv) * D * 2 * BH >= (1ll << 40))
+    return GFX906_B200_EINVAL;
+  // k and v may be empty (and then null) when Skv == 0; q and o hold data here.
+  if (!q || !o || (Skv > 0 && (!k || !v))) return GFX906_B200_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+       reinterpret_cast<uintptr_t>(o)) & 15u)
+    return GFX906_B200_EALIGN;
+  int dev = 0;
+  int rc = check_device(&dev);
+  if (rc != GFX906_B200_OK) return rc;
+  if (Skv == 0) {
+    // softmax over an empty key set: defined here as a zero output.
+    if (cudaMemsetAsync(o, 0, static_cast<size_t>(BH) * Sq * D * 2, stream) != cudaSuccess)
+      return GFX906_B200_ECUDA;
+    return GFX906_B200_OK;
+  }
+  if (D == 128) return launch_dp<128>(q, k, v, o, BH, Sq, Skv, D, scale, stream);
+  if (D <= 64) return launch_dp<64>(q, k, v, o, BH, Sq, Skv, D, scale, stream);
+  return GFX906_B200_EHEADDIM;  // D == 512 path not built yet
+}
+
+}  // namespace
+
+extern "C" {
+
+int gfx906_b200_attn_launch(const void* q, const void* k, const void* v, void* o, int B, int H, int Sq,
+                            int Skv, int D, float scale, cudaStream_t stream) {
+  const int rc = attn_launch_impl(q, k, v, o, B, H, Sq, Skv, D, scale, stream);
+  t_last_error = rc;
+  return rc;
+}
+
+void launch(const void* q, const void* k, const void* v, void* o, int B, int H, int Sq, int Skv, int D,
+            float scale, cudaStream_t stream) {
+  (void)gfx906_b200_attn_launch(q, k, v, o, B, H, Sq, Skv, D, scale, stream);
+}
+
+int gfx906_b200_attn_last_error(void) { return t_last_error; }
+
+const char* gfx906_b200_attn_error_string(int status) {
+  switch (status) {
+    case GFX906_B200_OK: return "ok";
+    case GFX906_B200_EINVAL: return "invalid argument (negative size, null pointer or size overflow)";
+    case GFX906_B200_EHEADDIM: return "unsupported head_dim (need <=64 and a multiple of 8, 128, or 512)";
+    case GFX906_B200_EALIGN: return "q, k, v and o must be 16-byte aligned";
+    case GFX906_B200_ENODEV: return "current CUDA device is not an sm_100 (B200) GPU";
+    case GFX906_B200_ECUDA: return "a CUDA runtime or driver call failed";
+    case GFX906_B200_ETIMEOUT: return "a kernel wait timed out (device status word set)";
+    default: return "unknown status";
+  }
+}
+
+int gfx906_b200_attn_device_status(int reset) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return GFX906_B200_ECUDA;
+  unsigned int st = 0;
+  if (cudaMemcpyFromSymbol(&st, fa::g_status, sizeof(st)) != cudaSuccess) return GFX906_B200_ECUDA;
+  if (reset) {
+    const unsigned int zero = 0;
+    int zeros[6] = {0, 0, 0, 0, 0, 0};
+    if (cudaMemcpyToSymbol(fa::g_status, &zero, sizeof(zero)) != cudaSuccess ||
+        cudaMemcpyToSymbol(fa::g_timeout_info, zeros, sizeof(zeros)) != cudaSuccess)
+      return GFX906_B200_ECUDA;
+  }
+  return st ? GFX906_B200_ETIMEOUT : GFX906_B200_OK;
+}
+
+int gfx906_b200_attn_timeout_info(int* out6) {
+  if (!out6) return GFX906_B200_EINVAL;
+  if (cudaDeviceSynchronize() != cudaSuccess) return GFX906_B200_ECUDA;
+  if (cudaMemcpyFromSymbol(out6, fa::g_timeout_info, 6 * sizeof(int)) != cudaSuccess) return GFX906_B200_ECUDA;
+  return GFX906_B200_OK;
+}
+
+int gfx906_b200_attn_selftest_wait_timeout(unsigned long long timeout_ns, cudaStream_t stream) {
+  int dev = 0;
+  int rc = check_device(&dev);
+  if (rc != GFX906_B200_OK) return rc;
+  fa::wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(timeout_ns);
+  return cudaGetLastError() == cudaSuccess ? GFX906_B200_OK : GFX906_B200_ECUDA;
+}
+
+double gfx906_b200_attn_flops(int B, int H, int Sq, int Skv, int D) {
+  return 4.0 * B * H * static_cast<double>(Sq) * Skv * D;
+}
+
+}  // extern "C"

@@ -1,0 +1,93 @@
+/*
+ * C ABI of the B200 (sm_100a) flash-attention forward path.
+ *
+ * Drop-in for the reference's kernel shim: the reference binds
+ *   extern "C" void launch(const void*, const void*, const void*, void*,
+ *                          int, int, int, int, int, float, hipStream_t);
+ * (attn_kernel.hip:710-711, declared again in attn.cpp:4-5). This library
+ * exports the same symbol with the same argument order and meaning, with a
+ * CUDA stream in place of the HIP stream, plus a status-returning form.
+ *
+ * Tensors: q [B,H,Sq,D], k and v [B,H,Skv,D], o [B,H,Sq,D]; fp16 (IEEE
+ * binary16), contiguous, device pointers, 16-byte aligned. The caller owns
+ * every buffer (the library allocates nothing per call). Work is enqueued
+ * asynchronously on `stream`; nothing synchronises.
+ * Supported head dims: D <= 64 with D % 8 == 0, D == 128, D == 512
+ * (the reference's envelope, attn.cpp:13-14).
+ * Skv == 0 writes zeros to o (the reference left such rows unwritten).
+ * Only sm_100 devices (B200) are accepted.
+ */
+#ifndef GFX906_B200_ATTN_H
+#define GFX906_B200_ATTN_H
+
+#include <cuda_runtime_api.h>
+
+#if defined(__GNUC__)
+#define GFX906_B200_API __attribute__((visibility("default")))
+#else
+#define GFX906_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by gfx906_b200_attn_launch. */
+#define GFX906_B200_OK 0
+#define GFX906_B200_EINVAL 1      /* negative size, null pointer, size overflow */
+#define GFX906_B200_EHEADDIM 2    /* D not in {8,16,...,64, 128, 512} */
+#define GFX906_B200_EALIGN 3      /* a pointer is not 16-byte aligned */
+#define GFX906_B200_ENODEV 4      /* current device is not sm_100 */
+#define GFX906_B200_ECUDA 5       /* a CUDA runtime or driver call failed */
+#define GFX906_B200_ETIMEOUT 6    /* a kernel wait ran out (device status word) */
+
+/* Replaces attn_kernel.hip:710-742 `launch` (same arguments; cudaStream_t for
+ * hipStream_t). Returns nothing, like the reference; the status of the call
+ * is kept for gfx906_b200_attn_last_error(). */
+GFX906_B200_API void launch(const void* q, const void* k, const void* v, void* o,
+            int B, int H, int Sq, int Skv, int D, float scale,
+            cudaStream_t stream);
+
+/* Same work as launch(); returns a GFX906_B200_* status instead of void.
+ * The reference's launch never checks its arguments or launch errors
+ * (attn_kernel.hip:710-742); this form reports both. */
+GFX906_B200_API int gfx906_b200_attn_launch(const void* q, const void* k, const void* v,
+                            void* o, int B, int H, int Sq, int Skv, int D,
+                            float scale, cudaStream_t stream);
+
+/* Status of the last launch()/gfx906_b200_attn_launch() on this host thread.
+ * No reference counterpart (the reference's launch returns void). */
+GFX906_B200_API int gfx906_b200_attn_last_error(void);
+
+/* Human-readable text for a GFX906_B200_* status. No reference counterpart. */
+GFX906_B200_API const char* gfx906_b200_attn_error_string(int status);
+
+/* Reads (and, if reset != 0, clears) the device status word of the current
+ * device, which a kernel sets when one of its bounded waits runs out.
+ * Synchronises the device. Returns GFX906_B200_OK or GFX906_B200_ETIMEOUT
+ * (GFX906_B200_ECUDA if the read itself fails). No reference counterpart:
+ * the reference's kernels have no waits that can time out. */
+GFX906_B200_API int gfx906_b200_attn_device_status(int reset);
+
+/* Diagnostics of the first timed-out wait since the last reset:
+ * out[0]=block x, out[1]=block y, out[2]=warp, out[3]=barrier index,
+ * out[4]=phase parity, out[5]=role. Synchronises. Returns a status. */
+GFX906_B200_API int gfx906_b200_attn_timeout_info(int* out6);
+
+/* Self-test of the bounded wait: launches one block that waits on an
+ * mbarrier nothing arrives at, with the given limit in nanoseconds. The
+ * block gives up, sets the device status word and exits, leaving the
+ * context usable. Used by the GPU tests of failure detection. No reference
+ * counterpart. */
+GFX906_B200_API int gfx906_b200_attn_selftest_wait_timeout(unsigned long long timeout_ns,
+                                           cudaStream_t stream);
+
+/* Floating-point operations of one call, 4*B*H*Sq*Skv*D, the reference's
+ * throughput formula (flops_probe.py:18). */
+GFX906_B200_API double gfx906_b200_attn_flops(int B, int H, int Sq, int Skv, int D);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GFX906_B200_ATTN_H */
