@@ -55,10 +55,21 @@ namespace fa {
 constexpr int BM = 128;            // query rows per tile (= TMEM lanes)
 constexpr int BN = 128;            // keys per K/V tile
 constexpr int CHUNK_BYTES = 16384; // one 128-row x 64-col fp16 swizzled box
-constexpr int NUM_THREADS = 320;   // 8 softmax warps + producer + MMA
+constexpr int NUM_THREADS = 384;   // 2 softmax warpgroups + 1 control warpgroup
+// Register split after launch (launch: 384 x 168 = 64512): the softmax
+// warpgroups hold a 128-column score row per thread; the control warpgroup
+// (producer, MMA issuer, two idle warps) needs fewer. 256*200 + 128*96 = 63488.
+constexpr uint32_t REGS_SOFTMAX = 200;
+constexpr uint32_t REGS_CONTROL = 96;
 constexpr int PRODUCER_WARP = 8;
 constexpr int MMA_WARP = 9;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+#ifndef ATTN_EMU_PAIRS
+#define ATTN_EMU_PAIRS 1
+#endif
+// Pairs of exponentials, out of every 4 pairs (8 columns), evaluated with the
+// FMA-pipe polynomial instead of MUFU ex2 (balances the two pipes).
+constexpr int EMU_PAIRS = ATTN_EMU_PAIRS;
 
 // Roles recorded in the timeout diagnostics.
 enum Role : int { ROLE_PRODUCER = 1, ROLE_MMA = 2, ROLE_SOFTMAX0 = 3, ROLE_SOFTMAX1 = 4 };
@@ -96,7 +107,7 @@ struct Cfg {
   static constexpr int B_EPI = B_DRAIN + 1;  // 2 barriers: staging written, per tile
 };
 
-__device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+__device__ __forceinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                        unsigned long long timeout_ns, int bar_idx, int role) {
   const uint64_t t0 = globaltimer_ns();
   uint32_t n = 0;
@@ -140,6 +151,51 @@ __device__ __forceinline__ bool bwait_warp(uint32_t bars, int idx, uint32_t pari
                                            int role) {
   const bool ok = bwait(bars, idx, parity, abort_flag, timeout_ns, role);
   return __all_sync(0xffffffffu, ok);
+}
+
+// P = exp2(s * sl2 + neg_m) for one 128-column score row, rounded to fp16 and
+// stored into TMEM columns [tS, tS + 64) (two fp16 per column); returns the
+// fp32 row sum in two partial sums. EMU_PAIRS of every 4 column pairs use the
+// FMA-pipe polynomial, the rest MUFU. MASK zeroes columns >= nvalid (last
+// key tile).
+template <bool MASK>
+__device__ __forceinline__ void row_exp_store(const uint32_t* s, float sl2, float neg_m, int nvalid,
+                                              uint32_t tS, float& sum0, float& sum1) {
+  const uint64_t sl2x2 = f2_pack(sl2, sl2);
+  const uint64_t negm2 = f2_pack(neg_m, neg_m);
+  uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t pk[32];
+#pragma unroll
+    for (int c2 = 0; c2 < 32; ++c2) {
+      const int c = h * 64 + 2 * c2;
+      const uint64_t X = f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2x2, negm2);
+      float x0, x1, e0, e1;
+      f2_unpack(X, x0, x1);
+      if ((c2 & 3) < EMU_PAIRS) {
+        exp2_poly3_x2(x0, x1, e0, e1);
+      } else {
+        e0 = ex2_approx(x0);
+        e1 = ex2_approx(x1);
+      }
+      if (MASK) {
+        e0 = (c < nvalid) ? e0 : 0.f;
+        e1 = (c + 1 < nvalid) ? e1 : 0.f;
+      }
+      if (c2 & 1)
+        acc1 = f2_add(acc1, f2_pack(e0, e1));
+      else
+        acc0 = f2_add(acc0, f2_pack(e0, e1));
+      pk[c2] = pack_half2(e0, e1);
+    }
+    tmem_st32(tS + 32 * h, pk);
+  }
+  float a, b, c, d;
+  f2_unpack(acc0, a, b);
+  f2_unpack(acc1, c, d);
+  sum0 = a + c;
+  sum1 = b + d;
 }
 
 template <int DP>
@@ -195,6 +251,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
   const unsigned long long tmo = p.timeout_ns;
 
+  if (warp >= 8) setmaxnreg_dec<REGS_CONTROL>();  // whole control warpgroup, one instruction
   if (warp == PRODUCER_WARP) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -252,19 +309,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t tS0 = tmem + 0, tS1 = tmem + 128;
       const uint32_t tO0 = tmem + 256, tO1 = tmem + 256 + DP;
 
-      auto issue_qk = [&](uint32_t d_tmem, uint32_t sQ, uint32_t sK) {
-        for (int k = 0; k < ksteps; ++k) {
-          const uint32_t off = (k >> 2) * CHUNK_BYTES + (k & 3) * 32;
-          mma_f16_ss(d_tmem, sdesc_sw128(sQ + off, 16, 1024), sdesc_sw128(sK + off, 16, 1024),
-                     IDESC_QK, k > 0 ? 1u : 0u);
+      // Descriptors are built once; an MMA step only adds its byte offset >> 4
+      // to the start-address field (all tiles lie below 256 KiB of shared
+      // memory, so the field never carries into the next one).
+      const uint64_t dQ0 = sdesc_sw128(sQ0, 16, 1024), dQ1 = sdesc_sw128(sQ1, 16, 1024);
+      const uint64_t dK = sdesc_sw128(sKV, 16, 1024);            // K-major K tiles
+      const uint64_t dV = sdesc_sw128(sKV, CHUNK_BYTES, 1024);   // MN-major V tiles
+      auto issue_qk = [&](uint32_t d_tmem, uint64_t dq, uint32_t kv_off) {
+#pragma unroll
+        for (int k = 0; k < DP / 16; ++k) {
+          const uint32_t off = static_cast<uint32_t>((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4;
+          if (DP == 128 || k < ksteps)
+            mma_f16_ss(d_tmem, dq + off, dK + ((kv_off >> 4) + off), IDESC_QK, k > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](uint32_t d_tmem, uint32_t p_tmem, uint32_t sV, bool acc) {
+      auto issue_pv = [&](uint32_t d_tmem, uint32_t p_tmem, uint32_t v_off, bool acc) {
 #pragma unroll
-        for (int k = 0; k < BN / 16; ++k) {
-          mma_f16_ts(d_tmem, p_tmem + 8 * k, sdesc_sw128(sV + k * 2048, CHUNK_BYTES, 1024), idesc_pv,
+        for (int k = 0; k < BN / 16; ++k)
+          mma_f16_ts(d_tmem, p_tmem + 8 * k, dV + ((v_off + k * 2048) >> 4), idesc_pv,
                      (acc || k > 0) ? 1u : 0u);
-        }
       };
 
       bool ok = bwait(bars, C::B_Q, 0, abort_flag, tmo, ROLE_MMA);
@@ -278,35 +341,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int v_slot = it % C::STAGES;
         const uint32_t v_ph = (it / C::STAGES) & 1;
         ++it;
-        const uint32_t sK = sKV + k_slot * C::TILE_BYTES;
-        const uint32_t sV = sKV + v_slot * C::TILE_BYTES;
 
         if (!bwait(bars, C::B_KV_FULL + k_slot, k_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
         tc_fence_after();
-        issue_qk(tS0, sQ0, sK);  // S0(j); PV0(j-1) was issued before it
+        issue_qk(tS0, dQ0, k_slot * C::TILE_BYTES);  // S0(j); PV0(j-1) was issued before it
         tc_commit(bars + 8 * (C::B_S_FULL + 0));
         if (has1) {
           if (j > 0) {
             if (!bwait(bars, C::B_P_FULL + 1, (j - 1) & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
             tc_fence_after();
-            issue_pv(tO1, tS1, sKV + prev_v_slot * C::TILE_BYTES, j - 1 > 0);
+            issue_pv(tO1, tS1, prev_v_slot * C::TILE_BYTES, j - 1 > 0);
             tc_commit(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));  // V(j-1) free
           }
-          issue_qk(tS1, sQ1, sK);
+          issue_qk(tS1, dQ1, k_slot * C::TILE_BYTES);
           tc_commit(bars + 8 * (C::B_S_FULL + 1));
         }
         tc_commit(bars + 8 * (C::B_KV_EMPTY + k_slot));  // K(j) free
         if (!bwait(bars, C::B_KV_FULL + v_slot, v_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
         if (!bwait(bars, C::B_P_FULL + 0, j & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
         tc_fence_after();
-        issue_pv(tO0, tS0, sV, j > 0);
+        issue_pv(tO0, tS0, v_slot * C::TILE_BYTES, j > 0);
         if (!has1) tc_commit(bars + 8 * (C::B_KV_EMPTY + v_slot));
         prev_v_slot = v_slot;
       }
       if (ok && has1 && n_tiles > 0) {
         if (bwait(bars, C::B_P_FULL + 1, (n_tiles - 1) & 1, abort_flag, tmo, ROLE_MMA)) {
           tc_fence_after();
-          issue_pv(tO1, tS1, sKV + prev_v_slot * C::TILE_BYTES, n_tiles - 1 > 0);
+          issue_pv(tO1, tS1, prev_v_slot * C::TILE_BYTES, n_tiles - 1 > 0);
           tc_commit(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));
         } else {
           ok = false;
@@ -322,8 +383,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     __syncwarp();
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------------------ softmax
+    setmaxnreg_inc<REGS_SOFTMAX>();
     const int ti = warp >> 2;  // query tile
     const int quad = warp & 3; // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
@@ -352,36 +414,40 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // Row extreme of the raw scores: max for scale >= 0, min for scale < 0,
         // so that extreme * scale is the max of the scaled scores.
         float mx;
-        {
-          float a0 = pos ? -INFINITY : INFINITY, a1 = a0, a2 = a0, a3 = a0;
-          if (full) {
-            if (pos) {
+        if (full) {
+          float a0 = __uint_as_float(s[0]), a1 = __uint_as_float(s[1]);
+          float a2 = __uint_as_float(s[2]), a3 = __uint_as_float(s[3]);
+          if (pos) {
 #pragma unroll
-              for (int c = 0; c < BN; c += 4) {
-                a0 = fmaxf(a0, __uint_as_float(s[c]));
-                a1 = fmaxf(a1, __uint_as_float(s[c + 1]));
-                a2 = fmaxf(a2, __uint_as_float(s[c + 2]));
-                a3 = fmaxf(a3, __uint_as_float(s[c + 3]));
+            for (int c = 4; c < BN; c += 8) {
+              a0 = fmax3(a0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
+              a1 = fmax3(a1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
+              if (c + 4 < BN) {
+                a2 = fmax3(a2, __uint_as_float(s[c + 4]), __uint_as_float(s[c + 5]));
+                a3 = fmax3(a3, __uint_as_float(s[c + 6]), __uint_as_float(s[c + 7]));
               }
-              mx = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
-            } else {
-#pragma unroll
-              for (int c = 0; c < BN; c += 4) {
-                a0 = fminf(a0, __uint_as_float(s[c]));
-                a1 = fminf(a1, __uint_as_float(s[c + 1]));
-                a2 = fminf(a2, __uint_as_float(s[c + 2]));
-                a3 = fminf(a3, __uint_as_float(s[c + 3]));
-              }
-              mx = fminf(fminf(a0, a1), fminf(a2, a3));
             }
+            mx = fmax3(fmaxf(a0, a1), a2, a3);
           } else {
 #pragma unroll
-            for (int c = 0; c < BN; ++c) {
-              const float x = __uint_as_float(s[c]);
-              if (c < nvalid) a0 = pos ? fmaxf(a0, x) : fminf(a0, x);
+            for (int c = 4; c < BN; c += 8) {
+              a0 = fmin3(a0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
+              a1 = fmin3(a1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
+              if (c + 4 < BN) {
+                a2 = fmin3(a2, __uint_as_float(s[c + 4]), __uint_as_float(s[c + 5]));
+                a3 = fmin3(a3, __uint_as_float(s[c + 6]), __uint_as_float(s[c + 7]));
+              }
             }
-            mx = a0;
+            mx = fmin3(fminf(a0, a1), a2, a3);
           }
+        } else {
+          float a0 = pos ? -INFINITY : INFINITY;
+#pragma unroll
+          for (int c = 0; c < BN; ++c) {
+            const float x = __uint_as_float(s[c]);
+            if (c < nvalid) a0 = pos ? fmaxf(a0, x) : fminf(a0, x);
+          }
+          mx = a0;
         }
         const float m_cand = mx * sl2;
         const float m_new = fmaxf(m_run, m_cand);
@@ -395,25 +461,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const float neg_m = -m_run;
         // P = exp2(s * scale*log2(e) - m) as fp16 into the first 64 columns of
         // S, written in two halves so that half of s[] is dead before the rest.
-        float lsum0 = 0.f, lsum1 = 0.f;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t pk[32];
-#pragma unroll
-          for (int c2 = 0; c2 < 32; ++c2) {
-            const int c = h * 64 + 2 * c2;
-            float e0 = ex2_approx(fmaf(__uint_as_float(s[c]), sl2, neg_m));
-            float e1 = ex2_approx(fmaf(__uint_as_float(s[c + 1]), sl2, neg_m));
-            if (!full) {
-              e0 = (c < nvalid) ? e0 : 0.f;
-              e1 = (c + 1 < nvalid) ? e1 : 0.f;
-            }
-            lsum0 += e0;
-            lsum1 += e1;
-            pk[c2] = pack_half2(e0, e1);
-          }
-          tmem_st32(tS + 32 * h, pk);
-        }
+        float lsum0, lsum1;
+        if (full)
+          row_exp_store<false>(s, sl2, neg_m, nvalid, tS, lsum0, lsum1);
+        else
+          row_exp_store<true>(s, sl2, neg_m, nvalid, tS, lsum0, lsum1);
         l_run += lsum0 + lsum1;
         // Rescale this warp's O rows when any of them moved its max. PV(j-1)
         // of this tile completed before S(j) was signalled, and PV(j) is only

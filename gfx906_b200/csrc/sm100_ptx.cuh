@@ -197,6 +197,17 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Warpgroup-wide register reallocation (all 128 threads of a warpgroup execute
+// it). The sum over warpgroups must stay within what the block launched with.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ------------------------------------------------------------------- math
 // MUFU base-2 exponential (PTX ex2.approx, flush-to-zero). exp2(-inf) = 0.
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -204,6 +215,63 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Three-input max / min (sm_100: one instruction for two reduction steps).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// ---- packed fp32x2 arithmetic (sm_100: one instruction for two lanes of work)
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x for two values on the FMA pipe, to take part of the exponentials off
+// MUFU. x = n + f with n = round(x) and f in [-0.5, 0.5]: adding 1.5 * 2^23
+// rounds x to an integer held in the low mantissa bits of t; 2^f comes from a
+// degree-3 polynomial fitted here by the Remez exchange algorithm for minimum
+// relative error on [-0.5, 0.5] (max relative error 7.5e-5, a third of the
+// fp16 half-ulp the result is rounded to); 2^n is added to the exponent field
+// by an integer add of n << 23. x is clamped to >= -126 so that the exponent
+// stays in range (values that small are 0 after rounding to fp16); x <= 127
+// is assumed.
+__device__ __forceinline__ void exp2_poly3_x2(float x0, float x1, float& e0, float& e1) {
+  const uint64_t X = f2_pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const uint64_t T = f2_add(X, f2_pack(12582912.0f, 12582912.0f));
+  const uint64_t N = f2_add(T, f2_pack(-12582912.0f, -12582912.0f));
+  const uint64_t F = f2_fma(N, f2_pack(-1.0f, -1.0f), X);
+  uint64_t P = f2_fma(f2_pack(5.5171669058e-02f, 5.5171669058e-02f), F,
+                      f2_pack(2.4261112219e-01f, 2.4261112219e-01f));
+  P = f2_fma(P, F, f2_pack(6.9326098546e-01f, 6.9326098546e-01f));
+  P = f2_fma(P, F, f2_pack(9.9992807354e-01f, 9.9992807354e-01f));
+  float p0, p1, t0, t1;
+  f2_unpack(P, p0, p1);
+  f2_unpack(T, t0, t1);
+  e0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  e1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
 // Packs two floats into fp16x2, round-to-nearest-even; `lo` in bits [0,16).
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
