@@ -153,6 +153,44 @@ __device__ __forceinline__ bool bwait_warp(uint32_t bars, int idx, uint32_t pari
   return __all_sync(0xffffffffu, ok);
 }
 
+// Max over the valid columns of a raw score row (min when the scale is
+// negative), so that extreme * scale is the row max of the scaled scores.
+__device__ __forceinline__ float row_extreme(const uint32_t* s, int nvalid, bool full, bool pos) {
+  if (full) {
+    float a0 = __uint_as_float(s[0]), a1 = __uint_as_float(s[1]);
+    float a2 = __uint_as_float(s[2]), a3 = __uint_as_float(s[3]);
+    if (pos) {
+#pragma unroll
+      for (int c = 4; c < BN; c += 8) {
+        a0 = fmax3(a0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
+        a1 = fmax3(a1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
+        if (c + 4 < BN) {
+          a2 = fmax3(a2, __uint_as_float(s[c + 4]), __uint_as_float(s[c + 5]));
+          a3 = fmax3(a3, __uint_as_float(s[c + 6]), __uint_as_float(s[c + 7]));
+        }
+      }
+      return fmax3(fmaxf(a0, a1), a2, a3);
+    }
+#pragma unroll
+    for (int c = 4; c < BN; c += 8) {
+      a0 = fmin3(a0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
+      a1 = fmin3(a1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
+      if (c + 4 < BN) {
+        a2 = fmin3(a2, __uint_as_float(s[c + 4]), __uint_as_float(s[c + 5]));
+        a3 = fmin3(a3, __uint_as_float(s[c + 6]), __uint_as_float(s[c + 7]));
+      }
+    }
+    return fmin3(fminf(a0, a1), a2, a3);
+  }
+  float a0 = pos ? -INFINITY : INFINITY;
+#pragma unroll
+  for (int c = 0; c < BN; ++c) {
+    const float x = __uint_as_float(s[c]);
+    if (c < nvalid) a0 = pos ? fmaxf(a0, x) : fminf(a0, x);
+  }
+  return a0;
+}
+
 // P = exp2(s * sl2 + neg_m) for one 128-column score row, rounded to fp16 and
 // stored into TMEM columns [tS, tS + 64) (two fp16 per column); returns the
 // fp32 row sum in two partial sums. EMU_PAIRS of every 4 column pairs use the
@@ -413,42 +451,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const bool full = nvalid == BN;
         // Row extreme of the raw scores: max for scale >= 0, min for scale < 0,
         // so that extreme * scale is the max of the scaled scores.
-        float mx;
-        if (full) {
-          float a0 = __uint_as_float(s[0]), a1 = __uint_as_float(s[1]);
-          float a2 = __uint_as_float(s[2]), a3 = __uint_as_float(s[3]);
-          if (pos) {
-#pragma unroll
-            for (int c = 4; c < BN; c += 8) {
-              a0 = fmax3(a0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
-              a1 = fmax3(a1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
-              if (c + 4 < BN) {
-                a2 = fmax3(a2, __uint_as_float(s[c + 4]), __uint_as_float(s[c + 5]));
-                a3 = fmax3(a3, __uint_as_float(s[c + 6]), __uint_as_float(s[c + 7]));
-              }
-            }
-            mx = fmax3(fmaxf(a0, a1), a2, a3);
-          } else {
-#pragma unroll
-            for (int c = 4; c < BN; c += 8) {
-              a0 = fmin3(a0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
-              a1 = fmin3(a1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
-              if (c + 4 < BN) {
-                a2 = fmin3(a2, __uint_as_float(s[c + 4]), __uint_as_float(s[c + 5]));
-                a3 = fmin3(a3, __uint_as_float(s[c + 6]), __uint_as_float(s[c + 7]));
-              }
-            }
-            mx = fmin3(fminf(a0, a1), a2, a3);
-          }
-        } else {
-          float a0 = pos ? -INFINITY : INFINITY;
-#pragma unroll
-          for (int c = 0; c < BN; ++c) {
-            const float x = __uint_as_float(s[c]);
-            if (c < nvalid) a0 = pos ? fmaxf(a0, x) : fminf(a0, x);
-          }
-          mx = a0;
-        }
+        const float mx = row_extreme(s, nvalid, full, pos);
         const float m_cand = mx * sl2;
         const float m_new = fmaxf(m_run, m_cand);
         const bool need = m_new > m_run + RESCALE_THRESHOLD;
@@ -530,6 +533,291 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ----------------------------------------------------------------- D = 512
+// Head dim 512 (the reference's VAE mid-block path, attn_kernel.hip:525-708).
+// An fp32 O tile of 128 rows x 512 columns fills all of TMEM, so a CTA owns
+// one 128-row query tile and one half (256 columns) of the head dim: blockIdx.x
+// = 2 * query tile + half. Both halves compute the full S = Q K^T (K = 512):
+// 1.5x the minimum tensor work, in exchange for no inter-CTA traffic.
+// Q stays resident (128 KiB); K and the V half stream through a ring of three
+// 32 KiB slots, each slot a [128 keys x 128 head-dim] tile (two swizzled 64-col
+// boxes): per key tile K0..K3 (head dims 0..511) then, one tile later, V0 V1
+// (this half's 256 head dims). TMEM: S double-buffered at [0,128) / [128,256),
+// O half at [256,512); P of tile j is written over the first 64 columns of
+// its S buffer. MMA order: S(0), S(1), PV(0), S(2), PV(1), ... so the tensor
+// core computes S(j+1) while the softmax warpgroup works on S(j).
+struct Cfg512 {
+  static constexpr int SLOTS = 3;
+  static constexpr int SLOT_BYTES = 2 * CHUNK_BYTES;
+  static constexpr int Q_BYTES = 8 * CHUNK_BYTES;
+  static constexpr int DATA_BYTES = Q_BYTES + SLOTS * SLOT_BYTES;
+  // Q, KV_FULL[3], KV_EMPTY[3], S_FULL[2], P_FULL[2], PV_DONE, O_FULL, DRAIN, EPI
+  static constexpr int B_Q = 0, B_KV_FULL = 1, B_KV_EMPTY = 1 + SLOTS, B_S_FULL = 1 + 2 * SLOTS;
+  static constexpr int B_P_FULL = B_S_FULL + 2, B_PV_DONE = B_P_FULL + 2, B_O_FULL = B_PV_DONE + 1;
+  static constexpr int B_DRAIN = B_O_FULL + 1, B_EPI = B_DRAIN + 1, NUM_BARS = B_EPI + 1;
+  static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int THREADS = 256;  // softmax warpgroup + control warpgroup
+};
+
+__global__ void __launch_bounds__(Cfg512::THREADS, 1)
+    attn_fwd_d512_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                         const Params p) {
+  using C = Cfg512;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t s0 = (raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (s0 - raw);
+  const uint32_t sQ = s0;
+  const uint32_t sRing = s0 + C::Q_BYTES;
+  const uint32_t bars = s0 + C::DATA_BYTES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::DATA_BYTES + C::NUM_BARS * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* drain_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int bh = blockIdx.y + p.bh_offset;
+  const int half = blockIdx.x & 1;
+  const int q_row0 = (blockIdx.x >> 1) * BM;
+  const int n_tiles = (p.Skv + BN - 1) / BN;
+  const unsigned long long tmo = p.timeout_ns;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bars + 8 * C::B_Q, 1);
+    for (int s = 0; s < C::SLOTS; ++s) {
+      mbar_init(bars + 8 * (C::B_KV_FULL + s), 1);
+      mbar_init(bars + 8 * (C::B_KV_EMPTY + s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bars + 8 * (C::B_S_FULL + i), 1);
+      mbar_init(bars + 8 * (C::B_P_FULL + i), BM);
+    }
+    mbar_init(bars + 8 * C::B_PV_DONE, 1);
+    mbar_init(bars + 8 * C::B_O_FULL, 1);
+    mbar_init(bars + 8 * C::B_DRAIN, 1);
+    mbar_init(bars + 8 * C::B_EPI, BM);
+    *abort_flag = 0;
+    *drain_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_o);
+      mbar_arrive_expect_tx(bars + 8 * C::B_Q, C::Q_BYTES);
+      for (int c = 0; c < 8; ++c) tma_load_3d(sQ + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q, c * 64, q_row0, bh);
+      int it = 0;
+      bool ok = true;
+      // slot order: K(0); then K(j), V(j-1) for j >= 1; then V(n-1)
+      auto load_slot = [&](const CUtensorMap* m, int key0, int d0) -> bool {
+        const int slot = it % C::SLOTS;
+        const uint32_t ph = (it / C::SLOTS) & 1;
+        if (!bwait(bars, C::B_KV_EMPTY + slot, ph ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) return false;
+        const uint32_t full = bars + 8 * (C::B_KV_FULL + slot);
+        mbar_arrive_expect_tx(full, C::SLOT_BYTES);
+        tma_load_3d(sRing + slot * C::SLOT_BYTES, m, full, d0, key0, bh);
+        tma_load_3d(sRing + slot * C::SLOT_BYTES + CHUNK_BYTES, m, full, d0 + 64, key0, bh);
+        ++it;
+        return true;
+      };
+      for (int j = 0; j <= n_tiles && ok; ++j) {
+        if (j < n_tiles)
+          for (int s = 0; s < 4 && ok; ++s) ok = load_slot(&tm_k, j * BN, 128 * s);
+        if (j > 0)
+          for (int s = 0; s < 2 && ok; ++s) ok = load_slot(&tm_v, (j - 1) * BN, 256 * half + 128 * s);
+      }
+      if (!ok) {
+        if (!mbar_try_wait(bars + 8 * C::B_Q, 0))
+          wait_slow(bars + 8 * C::B_Q, 0, drain_flag, 100000000ull, C::B_Q, ROLE_PRODUCER);
+        const int first = it > C::SLOTS ? it - C::SLOTS : 0;
+        for (int t = first; t < it; ++t) {
+          const int slot = t % C::SLOTS;
+          const uint32_t ph = (t / C::SLOTS) & 1;
+          if (!mbar_try_wait(bars + 8 * (C::B_KV_FULL + slot), ph))
+            wait_slow(bars + 8 * (C::B_KV_FULL + slot), ph, drain_flag, 100000000ull, C::B_KV_FULL + slot,
+                      ROLE_PRODUCER);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ----------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC_QK = idesc_f16_f32(BM, BN, 0, 0);
+      constexpr uint32_t IDESC_PV = idesc_f16_f32(BM, 128, 0, 1);
+      const uint64_t dQ = sdesc_sw128(sQ, 16, 1024);
+      const uint64_t dK = sdesc_sw128(sRing, 16, 1024);
+      const uint64_t dV = sdesc_sw128(sRing, CHUNK_BYTES, 1024);
+      const uint32_t tO = tmem + 256;
+      int it = 0;
+      bool ok = bwait(bars, C::B_Q, 0, abort_flag, tmo, ROLE_MMA);
+      tc_fence_after();
+      auto next_slot = [&](int& slot) -> bool {
+        slot = it % C::SLOTS;
+        const uint32_t ph = (it / C::SLOTS) & 1;
+        ++it;
+        if (!bwait(bars, C::B_KV_FULL + slot, ph, abort_flag, tmo, ROLE_MMA)) return false;
+        tc_fence_after();
+        return true;
+      };
+      auto issue_s = [&](int j) -> bool {
+        const uint32_t tS = tmem + 128 * (j & 1);
+        for (int s = 0; s < 4; ++s) {
+          int slot;
+          if (!next_slot(slot)) return false;
+          const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t qoff = static_cast<uint32_t>((2 * s + (k >> 2)) * CHUNK_BYTES + (k & 3) * 32) >> 4;
+            const uint32_t koff = soff + (static_cast<uint32_t>((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4);
+            mma_f16_ss(tS, dQ + qoff, dK + koff, IDESC_QK, (s > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(bars + 8 * (C::B_KV_EMPTY + slot));
+        }
+        tc_commit(bars + 8 * (C::B_S_FULL + (j & 1)));
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        if (!bwait(bars, C::B_P_FULL + (j & 1), (j >> 1) & 1, abort_flag, tmo, ROLE_MMA)) return false;
+        tc_fence_after();
+        const uint32_t tP = tmem + 128 * (j & 1);
+        for (int s = 0; s < 2; ++s) {
+          int slot;
+          if (!next_slot(slot)) return false;
+          const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
+#pragma unroll
+          for (int k = 0; k < BN / 16; ++k)
+            mma_f16_ts(tO + 128 * s, tP + 8 * k, dV + soff + ((k * 2048) >> 4), IDESC_PV,
+                       (j > 0 || k > 0) ? 1u : 0u);
+          tc_commit(bars + 8 * (C::B_KV_EMPTY + slot));
+        }
+        tc_commit(bars + 8 * C::B_PV_DONE);
+        return true;
+      };
+      for (int j = 0; j <= n_tiles && ok; ++j) {
+        if (j < n_tiles) ok = issue_s(j);
+        if (ok && j > 0) ok = issue_pv(j - 1);
+      }
+      if (ok) {
+        tc_commit(bars + 8 * C::B_O_FULL);
+      } else {
+        tc_commit(bars + 8 * C::B_DRAIN);
+        wait_slow(bars + 8 * C::B_DRAIN, 0, drain_flag, 100000000ull, C::B_DRAIN, ROLE_MMA);
+      }
+    }
+    __syncwarp();
+  } else if (warp < 4) {
+    // ------------------------------------------------------------- softmax
+    const int row = warp * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tO = tmem + lane_off + 256;
+    const float sl2 = p.scale_log2;
+    const bool pos = sl2 >= 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int b = j & 1;
+      const uint32_t tS = tmem + lane_off + 128 * b;
+      if (!bwait_warp(bars, C::B_S_FULL + b, (j >> 1) & 1, abort_flag, tmo, ROLE_SOFTMAX0)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + 32 * c, s + 32 * c);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) reg_fence32(s + 32 * c);
+      const int nvalid = min(BN, p.Skv - j * BN);
+      const bool full = nvalid == BN;
+      const float mx = row_extreme(s, nvalid, full, pos);
+      const float m_new = fmaxf(m_run, mx * sl2);
+      const bool need = m_new > m_run + RESCALE_THRESHOLD;
+      float factor = 1.f;
+      if (need) {
+        factor = ex2_approx(m_run - m_new);
+        m_run = m_new;
+      }
+      l_run *= factor;
+      float lsum0, lsum1;
+      if (full)
+        row_exp_store<false>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1);
+      else
+        row_exp_store<true>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1);
+      l_run += lsum0 + lsum1;
+      // O may only be rescaled once PV(j-1) has completed.
+      if (j > 0) {
+        if (!bwait_warp(bars, C::B_PV_DONE, (j - 1) & 1, abort_flag, tmo, ROLE_SOFTMAX0)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+          for (int c = 0; c < 256 / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + 32 * c, o);
+            tmem_wait_ld();
+            reg_fence32(o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+            tmem_st32(tO + 32 * c, o);
+          }
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bars + 8 * (C::B_P_FULL + b));
+    }
+    const bool have_o = ok && n_tiles > 0 && bwait_warp(bars, C::B_O_FULL, 0, abort_flag, tmo, ROLE_SOFTMAX0);
+    if (have_o) {
+      tc_fence_after();
+      const float inv = 1.f / l_run;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[64];
+        tmem_ld32(tO + 64 * c, o);
+        tmem_ld32(tO + 64 * c + 32, o + 32);
+        tmem_wait_ld();
+        reg_fence32(o);
+        reg_fence32(o + 32);
+        const uint32_t rowbase = sQ + c * CHUNK_BYTES + row * 128;  // Q is dead: its last MMA completed
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint32_t a = pack_half2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
+          const uint32_t bb = pack_half2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
+          const uint32_t cc = pack_half2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
+          const uint32_t d = pack_half2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
+          st_shared_v4(rowbase + ((u ^ (row & 7)) << 4), a, bb, cc, d);
+        }
+      }
+      fence_proxy_async_smem();
+    }
+    mbar_arrive(bars + 8 * C::B_EPI);
+    if (warp == 0 && lane == 0 && have_o && bwait(bars, C::B_EPI, 0, abort_flag, tmo, ROLE_SOFTMAX0)) {
+      for (int c = 0; c < 4; ++c) tma_store_3d(&tm_o, sQ + c * CHUNK_BYTES, 256 * half + 64 * c, q_row0, bh);
+      tma_store_commit();
+      tma_store_wait_read0();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -618,7 +906,9 @@ int check_device(int* dev_out) {
     if (cudaFuncSetAttribute(fa::attn_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              fa::Cfg<64>::SMEM_BYTES) != cudaSuccess ||
         cudaFuncSetAttribute(fa::attn_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             fa::Cfg<128>::SMEM_BYTES) != cudaSuccess)
+                             fa::Cfg<128>::SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(fa::attn_fwd_d512_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             fa::Cfg512::SMEM_BYTES) != cudaSuccess)
       return GFX906_B200_ECUDA;
     di.attrs_set = true;
   }
@@ -660,6 +950,29 @@ int launch_dp(const void* q, const void* k, const void* v, void* o, long long BH
   return GFX906_B200_OK;
 }
 
+int launch_d512(const void* q, const void* k, const void* v, void* o, long long BH, int Sq, int Skv,
+                float scale, cudaStream_t stream) {
+  CUtensorMap mq, mk, mv, mo;
+  if (!make_map(&mq, q, 512, Sq, BH, fa::BM) || !make_map(&mk, k, 512, Skv, BH, fa::BN) ||
+      !make_map(&mv, v, 512, Skv, BH, fa::BN) || !make_map(&mo, o, 512, Sq, BH, fa::BM))
+    return GFX906_B200_ECUDA;
+  fa::Params prm;
+  prm.Sq = Sq;
+  prm.Skv = Skv;
+  prm.D = 512;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.timeout_ns = timeout_ns_from_env();
+  const unsigned qtiles = static_cast<unsigned>((Sq + fa::BM - 1) / fa::BM);
+  for (long long off = 0; off < BH; off += 65535) {
+    const long long n = (BH - off) < 65535 ? (BH - off) : 65535;
+    prm.bh_offset = static_cast<int>(off);
+    dim3 grid(2 * qtiles, static_cast<unsigned>(n), 1);
+    fa::attn_fwd_d512_kernel<<<grid, fa::Cfg512::THREADS, fa::Cfg512::SMEM_BYTES, stream>>>(mq, mk, mv, mo, prm);
+    if (cudaGetLastError() != cudaSuccess) return GFX906_B200_ECUDA;
+  }
+  return GFX906_B200_OK;
+}
+
 int attn_launch_impl(const void* q, const void* k, const void* v, void* o, int B, int H, int Sq, int Skv,
                      int D, float scale, cudaStream_t stream) {
   if (B < 0 || H < 0 || Sq < 0 || Skv < 0) return GFX906_B200_EINVAL;
@@ -685,7 +998,7 @@ int attn_launch_impl(const void* q, const void* k, const void* v, void* o, int B
   }
   if (D == 128) return launch_dp<128>(q, k, v, o, BH, Sq, Skv, D, scale, stream);
   if (D <= 64) return launch_dp<64>(q, k, v, o, BH, Sq, Skv, D, scale, stream);
-  return GFX906_B200_EHEADDIM;  // D == 512 path not built yet
+  return launch_d512(q, k, v, o, BH, Sq, Skv, scale, stream);
 }
 
 }  // namespace

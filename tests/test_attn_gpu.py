@@ -32,8 +32,6 @@ def run(op, q, k, v, scale):
 def test_golden_reference_model_cases(op, golden):
     """Kernel vs the reference's own pair-kernel model (model_check.py:103-133)."""
     for name, c in golden.items():
-        if c["q"].shape[-1] == 512:
-            continue
         q, k, v = (torch.from_numpy(c[x]) for x in ("q", "k", "v"))
         out = run(op, q, k, v, float(c["scale"])).float().numpy()
         ref = c["out"]
@@ -63,7 +61,7 @@ def test_small_head_dims(op, D):
 
 @pytest.mark.parametrize("Sq,Skv,D", [(256, 256, 64), (1024, 1024, 64), (100, 300, 64),
                                       (256, 256, 128), (1024, 1024, 128), (77, 411, 128),
-                                      (512, 512, 32)])
+                                      (512, 512, 32), (512, 512, 512)])
 def test_reference_variant_matrix(op, Sq, Skv, D):
     """test_variants.py:78-80 shapes (B=2, H=4, scale 0.125): Sq != Skv, odd lengths."""
     q, k, v = make_qkv(2, 4, Sq, Skv, D, seed=Sq + Skv + D)
@@ -80,7 +78,7 @@ def test_ragged_edges(op, Sq, Skv, D):
     check_rows(out, q, k, v, D ** -0.5, what=f"{Sq}x{Skv} D{D}")
 
 
-@pytest.mark.parametrize("name", ["C1", "C2", "C3", "C5s"])
+@pytest.mark.parametrize("name", ["C1", "C2", "C3", "C4", "C5s"])
 def test_benchmark_configs(op, name):
     cfg = CONFIGS[name]
     q, k, v = config_inputs(cfg)
@@ -177,3 +175,31 @@ def test_long_sequence_memory_is_linear(op):
     assert peak <= out.numel() * 2 + (1 << 20), peak
     rows = sample_rows(S, n_each=64, seed=14)
     check_rows(out.cpu(), q.cpu(), k.cpu(), v.cpu(), 0.125, rows, what="S=32768")
+
+
+@pytest.mark.parametrize("S", [256, 1024, 4096, 9216])
+def test_reference_d512_shapes(op, S):
+    """test_d512.py:19-20: D=512, one head, checked on a <=1024-row slice."""
+    q, k, v = make_qkv(1, 1, S, S, 512, seed=S + 512)
+    out = run(op, q, k, v, 512 ** -0.5)
+    rows = None if S <= 1024 else sample_rows(S, seed=S)
+    check_rows(out, q, k, v, 512 ** -0.5, rows, what=f"D512 S={S}")
+
+
+@pytest.mark.parametrize("Sq,Skv", [(1, 1), (77, 411), (130, 129), (300, 1000), (1000, 64)])
+def test_d512_ragged(op, Sq, Skv):
+    q, k, v = make_qkv(2, 2, Sq, Skv, 512, seed=Sq * 3 + Skv)
+    out = run(op, q, k, v, 512 ** -0.5)
+    check_rows(out, q, k, v, 512 ** -0.5, what=f"D512 {Sq}x{Skv}")
+
+
+def test_d512_non_contiguous_vae_layout(op):
+    """test_d512.py:22-30: strided q and transposed [b, D, S] k/v views."""
+    g = torch.Generator().manual_seed(21)
+    b, S, D = 1, 1024, 512
+    qf = torch.randn(b, S, D * 2, generator=g).half()[:, :, ::2]
+    kf = torch.randn(b, D, S, generator=g).half().transpose(1, 2)
+    vf = torch.randn(b, D, S, generator=g).half().transpose(1, 2)
+    q4, k4, v4 = qf.unsqueeze(1), kf.unsqueeze(1), vf.unsqueeze(1)
+    out = op.attn(q4.cuda(), k4.cuda(), v4.cuda(), D ** -0.5).cpu()
+    check_rows(out, q4.contiguous(), k4.contiguous(), v4.contiguous(), D ** -0.5, what="d512 noncontig")
