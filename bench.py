@@ -369,15 +369,22 @@ def _launches_per_call(cfg: AttnConfig) -> int:
 
 
 def _c_launcher():
-    """Direct C-ABI launch on preallocated outputs (no allocation in the timed loop)."""
+    """Direct C-ABI launch on preallocated outputs and workspace (no allocation
+    in the timed loop): the split schedule the torch op uses."""
     from gfx906_b200 import build
     from gfx906_b200.cabi import CABI
 
     lib = CABI(build.LIB_PATH)
+    cache = {}
 
     def launch(q, k, v, o, cfg, scale, stream):
-        return lib.launch_status(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), cfg.B,
-                                 cfg.H, cfg.Sq, cfg.Skv, cfg.D, scale, stream.cuda_stream)
+        n = lib.workspace_size(cfg.B, cfg.H, cfg.Sq, cfg.Skv, cfg.D)
+        ws = cache.get(q.device)
+        if n and (ws is None or ws.numel() < n):
+            ws = cache[q.device] = torch.zeros(n, dtype=torch.uint8, device=q.device)
+        return lib.launch_ws_status(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), cfg.B, cfg.H,
+                                    cfg.Sq, cfg.Skv, cfg.D, scale, ws.data_ptr() if n else None, n,
+                                    stream.cuda_stream)
 
     return launch
 

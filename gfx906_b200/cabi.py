@@ -34,11 +34,22 @@ class CABI:
         d.gfx906_b200_attn_timeout_info.restype = _c_int
         d.gfx906_b200_attn_selftest_wait_timeout.argtypes = [ctypes.c_ulonglong, _c_void_p]
         d.gfx906_b200_attn_selftest_wait_timeout.restype = _c_int
+        d.gfx906_b200_attn_workspace_size.argtypes = [_c_int] * 5
+        d.gfx906_b200_attn_workspace_size.restype = ctypes.c_size_t
+        d.gfx906_b200_attn_launch_ws.argtypes = sig[:-1] + [_c_void_p, ctypes.c_size_t, _c_void_p]
+        d.gfx906_b200_attn_launch_ws.restype = _c_int
         d.gfx906_b200_attn_flops.argtypes = [_c_int] * 5
         d.gfx906_b200_attn_flops.restype = ctypes.c_double
 
     def launch_status(self, q, k, v, o, B, H, Sq, Skv, D, scale, stream=None) -> int:
         return self.dll.gfx906_b200_attn_launch(q, k, v, o, B, H, Sq, Skv, D, _c_float(scale), stream)
+
+    def launch_ws_status(self, q, k, v, o, B, H, Sq, Skv, D, scale, ws, ws_bytes, stream=None) -> int:
+        return self.dll.gfx906_b200_attn_launch_ws(q, k, v, o, B, H, Sq, Skv, D, _c_float(scale), ws,
+                                                   ws_bytes, stream)
+
+    def workspace_size(self, B, H, Sq, Skv, D) -> int:
+        return self.dll.gfx906_b200_attn_workspace_size(B, H, Sq, Skv, D)
 
     def error_string(self, status: int) -> str:
         return self.dll.gfx906_b200_attn_error_string(status).decode()

@@ -12,7 +12,27 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "../../include/gfx906_b200_attn.h"
+
+// One workspace per (device, stream), reused by every call on that stream and
+// grown on demand. A workspace is never shared by two streams, so calls that
+// overlap on the GPU never share one.
+static std::mutex g_ws_mu;
+static std::map<std::pair<int, cudaStream_t>, torch::Tensor> g_ws;
+
+static torch::Tensor workspace_for(const torch::Tensor& like, cudaStream_t stream, size_t bytes) {
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  auto key = std::make_pair(static_cast<int>(like.get_device()), stream);
+  auto it = g_ws.find(key);
+  if (it != g_ws.end() && static_cast<size_t>(it->second.numel()) >= bytes) return it->second;
+  auto t = torch::empty({static_cast<int64_t>(bytes)}, like.options().dtype(torch::kUInt8));
+  g_ws[key] = t;
+  return t;
+}
 
 torch::Tensor attn(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale) {
   TORCH_CHECK(q.is_cuda() && q.dtype() == torch::kHalf, "kernel: q must be a CUDA float16 tensor");
@@ -32,10 +52,16 @@ torch::Tensor attn(torch::Tensor q, torch::Tensor k, torch::Tensor v, double sca
               "kernel: sizes must fit in int32");
   auto qc = q.contiguous(), kc = k.contiguous(), vc = v.contiguous();
   auto o = torch::empty_like(qc);
-  const int rc = gfx906_b200_attn_launch(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(),
-                                         static_cast<int>(B), static_cast<int>(H), static_cast<int>(Sq),
-                                         static_cast<int>(Skv), static_cast<int>(D),
-                                         static_cast<float>(scale), at::cuda::getCurrentCUDAStream());
+  const cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const size_t ws_bytes = gfx906_b200_attn_workspace_size(static_cast<int>(B), static_cast<int>(H),
+                                                          static_cast<int>(Sq), static_cast<int>(Skv),
+                                                          static_cast<int>(D));
+  void* ws = nullptr;
+  if (ws_bytes > 0) ws = workspace_for(q, stream, ws_bytes).data_ptr();
+  const int rc = gfx906_b200_attn_launch_ws(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(),
+                                            static_cast<int>(B), static_cast<int>(H), static_cast<int>(Sq),
+                                            static_cast<int>(Skv), static_cast<int>(D),
+                                            static_cast<float>(scale), ws, ws_bytes, stream);
   TORCH_CHECK(rc == GFX906_B200_OK, "kernel: ", gfx906_b200_attn_error_string(rc));
   return o;
 }

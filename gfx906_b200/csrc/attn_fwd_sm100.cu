@@ -45,6 +45,7 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "../../include/gfx906_b200_attn.h"
@@ -83,9 +84,20 @@ struct Params {
   int Sq;
   int Skv;
   int D;            // true head dim (<= DP)
-  int bh_offset;    // added to blockIdx.y
+  int bh_offset;    // added to blockIdx.y (D = 512 kernel)
   float scale_log2; // scale * log2(e)
   unsigned long long timeout_ns;
+  // persistent schedule of attn_fwd_kernel
+  int n_qb;               // 256-row query blocks per (batch, head)
+  int n_units;            // n_qb * B * H
+  int n_tiles;            // 128-key tiles per unit
+  int split;              // 1: stream-K split of the key range; 0: whole units
+  long long total_steps;  // n_units * n_tiles
+  __half* o;              // output, [B*H, Sq, D] fp16
+  float* ws_o;            // split workspace: [G][2][2][128][DP] partial O
+  float* ws_ml;           // [G][2][2][128][2] partial (m, l)
+  unsigned long long* ws_cnt;  // [n_units][2] arrival counters: (epoch << 8) | arrivals
+  unsigned long long epoch;    // unique per launch (56 bits), tags the counters
 };
 
 template <int DP>
@@ -93,18 +105,19 @@ struct Cfg {
   static constexpr int NCHUNK = DP / 64;
   static constexpr int TILE_BYTES = NCHUNK * CHUNK_BYTES;
   static constexpr int STAGES = (DP == 128) ? 4 : 8;
-  static constexpr int NUM_BARS = 1 + 2 * STAGES + 2 + 2 + 2 + 1 + 2;
-  static constexpr int DATA_BYTES = (2 + STAGES) * TILE_BYTES;
-  static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + DATA_BYTES + NUM_BARS * 8 + 16;
   // barrier indices
-  static constexpr int B_Q = 0;
-  static constexpr int B_KV_FULL = 1;
-  static constexpr int B_KV_EMPTY = 1 + STAGES;
-  static constexpr int B_S_FULL = 1 + 2 * STAGES;
+  static constexpr int B_Q_FULL = 0;
+  static constexpr int B_Q_EMPTY = 1;
+  static constexpr int B_KV_FULL = 2;
+  static constexpr int B_KV_EMPTY = 2 + STAGES;
+  static constexpr int B_S_FULL = 2 + 2 * STAGES;
   static constexpr int B_P_FULL = B_S_FULL + 2;
   static constexpr int B_O_FULL = B_P_FULL + 2;
-  static constexpr int B_DRAIN = B_O_FULL + 2;
-  static constexpr int B_EPI = B_DRAIN + 1;  // 2 barriers: staging written, per tile
+  static constexpr int B_WG = B_O_FULL + 2;  // per-warpgroup rendezvous, 2 barriers
+  static constexpr int B_DRAIN = B_WG + 2;
+  static constexpr int NUM_BARS = B_DRAIN + 1;
+  static constexpr int DATA_BYTES = (2 + STAGES) * TILE_BYTES;
+  static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + DATA_BYTES + NUM_BARS * 8 + 32;
 };
 
 __device__ __forceinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
@@ -151,6 +164,22 @@ __device__ __forceinline__ bool bwait_warp(uint32_t bars, int idx, uint32_t pari
                                            int role) {
   const bool ok = bwait(bars, idx, parity, abort_flag, timeout_ns, role);
   return __all_sync(0xffffffffu, ok);
+}
+
+// Stores columns [c0, c0 + 32) of one output row as fp16, o[e] * inv, keeping
+// only the first D columns (D is a multiple of 8, so stores stay 16-byte).
+__device__ __forceinline__ void store_row_f16(__half* orow, int c0, int D, const uint32_t* o, float inv) {
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    if (c0 + 8 * e < D) {
+      uint4 v;
+      v.x = pack_half2(__uint_as_float(o[8 * e + 0]) * inv, __uint_as_float(o[8 * e + 1]) * inv);
+      v.y = pack_half2(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv);
+      v.z = pack_half2(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv);
+      v.w = pack_half2(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv);
+      *reinterpret_cast<uint4*>(orow + c0 + 8 * e) = v;
+    }
+  }
 }
 
 // Max over the valid columns of a raw score row (min when the scale is
@@ -236,11 +265,67 @@ __device__ __forceinline__ void row_exp_store(const uint32_t* s, float sl2, floa
   sum1 = b + d;
 }
 
+// Persistent schedule shared by every role of attn_fwd_kernel: a CTA walks a
+// list of segments (unit, first key tile, end key tile). A unit is one
+// 256-row query block of one (batch, head). In split mode CTA c owns the
+// contiguous range [c*W/G, (c+1)*W/G) of the W = units * key-tiles steps, so
+// work is balanced to one key tile; a unit whose key range spans several CTAs
+// is computed as partial pieces that are combined by the last one to finish.
+// In whole mode CTA c takes units c, c+G, c+2G, ... (no partials).
+struct SegIter {
+  long long s, s_end;
+  int u, u_step, T, U;
+  bool split, first;
+  __device__ __forceinline__ void init(const Params& p, int c, int G) {
+    split = p.split != 0;
+    T = p.n_tiles;
+    U = p.n_units;
+    first = true;
+    if (split) {
+      s = static_cast<long long>(c) * p.total_steps / G;
+      s_end = static_cast<long long>(c + 1) * p.total_steps / G;
+    } else {
+      u = c;
+      u_step = G;
+    }
+  }
+  __device__ __forceinline__ bool next(int& unit, int& t0, int& t1, bool& first_seg) {
+    if (split) {
+      if (s >= s_end) return false;
+      unit = static_cast<int>(s / T);
+      const long long ubase = static_cast<long long>(unit) * T;
+      const long long e = (s_end < ubase + T) ? s_end : ubase + T;
+      t0 = static_cast<int>(s - ubase);
+      t1 = static_cast<int>(e - ubase);
+      s = e;
+    } else {
+      if (u >= U) return false;
+      unit = u;
+      t0 = 0;
+      t1 = T;
+      u += u_step;
+    }
+    first_seg = first;
+    first = false;
+    return true;
+  }
+};
+
+__device__ __forceinline__ long long range_begin(long long W, int G, int c) {
+  return static_cast<long long>(c) * W / G;
+}
+// Index of the CTA whose step range contains `step` (split mode).
+__device__ __forceinline__ int owner_cta(long long step, long long W, int G) {
+  int c = static_cast<int>((step * G) / W);
+  while (c + 1 < G && range_begin(W, G, c + 1) <= step) ++c;
+  while (c > 0 && range_begin(W, G, c) > step) --c;
+  return c;
+}
+
 template <int DP>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                    const Params p) {
+                    const __grid_constant__ CUtensorMap tm_v, const Params p) {
   using C = Cfg<DP>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -253,16 +338,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::DATA_BYTES + C::NUM_BARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* drain_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);  // stays 0
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 3);   // [2], per tile
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int bh = blockIdx.y + p.bh_offset;
-  const int q_row0 = blockIdx.x * (2 * BM);
-  const int n_tiles = (p.Skv + BN - 1) / BN;
-  const bool has1 = (q_row0 + BM) < p.Sq;  // second query tile has live rows
+  const int G = gridDim.x;
+  const int cta = blockIdx.x;
 
   if (threadIdx.x == 0) {
-    mbar_init(bars + 8 * C::B_Q, 1);
+    mbar_init(bars + 8 * C::B_Q_FULL, 1);
+    mbar_init(bars + 8 * C::B_Q_EMPTY, 1);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bars + 8 * (C::B_KV_FULL + s), 1);
       mbar_init(bars + 8 * (C::B_KV_EMPTY + s), 1);
@@ -271,7 +356,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(bars + 8 * (C::B_S_FULL + i), 1);
       mbar_init(bars + 8 * (C::B_P_FULL + i), BM);
       mbar_init(bars + 8 * (C::B_O_FULL + i), 1);
-      mbar_init(bars + 8 * (C::B_EPI + i), BM);
+      mbar_init(bars + 8 * (C::B_WG + i), BM);
+      last_flag[i] = 0;
     }
     mbar_init(bars + 8 * C::B_DRAIN, 1);
     *abort_flag = 0;
@@ -291,54 +377,68 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (warp >= 8) setmaxnreg_dec<REGS_CONTROL>();  // whole control warpgroup, one instruction
   if (warp == PRODUCER_WARP) {
+    // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      tma_prefetch_desc(&tm_o);
-      mbar_arrive_expect_tx(bars + 8 * C::B_Q, (has1 ? 2 : 1) * C::TILE_BYTES);
-#pragma unroll
-      for (int c = 0; c < C::NCHUNK; ++c) {
-        tma_load_3d(sQ0 + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q, c * 64, q_row0, bh);
-        if (has1)
-          tma_load_3d(sQ1 + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q, c * 64, q_row0 + BM, bh);
-      }
-      int it = 0;
+      SegIter si;
+      si.init(p, cta, G);
+      int unit, t0, t1;
+      bool fs;
+      int it = 0, qseg = 0, q_issued = 0;
       bool ok = true;
-      for (int j = 0; j < n_tiles && ok; ++j) {
+      while (ok && si.next(unit, t0, t1, fs)) {
+        const int bh = unit / p.n_qb;
+        const int q_row0 = (unit - bh * p.n_qb) * (2 * BM);
+        const bool has1 = (q_row0 + BM) < p.Sq;
+        // The Q buffers are free once every S MMA of the previous segment is done.
+        if (!bwait(bars, C::B_Q_EMPTY, (qseg & 1) ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx(bars + 8 * C::B_Q_FULL, (has1 ? 2 : 1) * C::TILE_BYTES);
 #pragma unroll
-        for (int kv = 0; kv < 2; ++kv) {
-          const int slot = it % C::STAGES;
-          const uint32_t ph = (it / C::STAGES) & 1;
-          if (!bwait(bars, C::B_KV_EMPTY + slot, ph ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) {
-            ok = false;
-            break;
+        for (int c = 0; c < C::NCHUNK; ++c) {
+          tma_load_3d(sQ0 + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q_FULL, c * 64, q_row0, bh);
+          if (has1)
+            tma_load_3d(sQ1 + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q_FULL, c * 64, q_row0 + BM, bh);
+        }
+        ++qseg;
+        q_issued = 1;
+        for (int j = t0; j < t1 && ok; ++j) {
+#pragma unroll
+          for (int kv = 0; kv < 2; ++kv) {
+            const int slot = it % C::STAGES;
+            const uint32_t ph = (it / C::STAGES) & 1;
+            if (!bwait(bars, C::B_KV_EMPTY + slot, ph ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) {
+              ok = false;
+              break;
+            }
+            const uint32_t full = bars + 8 * (C::B_KV_FULL + slot);
+            mbar_arrive_expect_tx(full, C::TILE_BYTES);
+            const CUtensorMap* m = kv ? &tm_v : &tm_k;
+#pragma unroll
+            for (int c = 0; c < C::NCHUNK; ++c)
+              tma_load_3d(sKV + slot * C::TILE_BYTES + c * CHUNK_BYTES, m, full, c * 64, j * BN, bh);
+            ++it;
           }
-          const uint32_t full = bars + 8 * (C::B_KV_FULL + slot);
-          mbar_arrive_expect_tx(full, C::TILE_BYTES);
-          const CUtensorMap* m = kv ? &tm_v : &tm_k;
-#pragma unroll
-          for (int c = 0; c < C::NCHUNK; ++c)
-            tma_load_3d(sKV + slot * C::TILE_BYTES + c * CHUNK_BYTES, m, full, c * 64, j * BN, bh);
-          ++it;
         }
       }
       if (!ok) {
         // Drain: every load issued must land before the CTA's shared memory goes away.
-        if (!mbar_try_wait(bars + 8 * C::B_Q, 0))
-          wait_slow(bars + 8 * C::B_Q, 0, drain_flag, 100000000ull, C::B_Q, ROLE_PRODUCER);
+        if (q_issued && !mbar_try_wait(bars + 8 * C::B_Q_FULL, (qseg - 1) & 1))
+          wait_slow(bars + 8 * C::B_Q_FULL, (qseg - 1) & 1, drain_flag, 100000000ull, C::B_Q_FULL, ROLE_PRODUCER);
         const int first = it > C::STAGES ? it - C::STAGES : 0;
         for (int t = first; t < it; ++t) {
           const int slot = t % C::STAGES;
           const uint32_t ph = (t / C::STAGES) & 1;
           if (!mbar_try_wait(bars + 8 * (C::B_KV_FULL + slot), ph))
-            wait_slow(bars + 8 * (C::B_KV_FULL + slot), ph, drain_flag, 100000000ull,
-                      C::B_KV_FULL + slot, ROLE_PRODUCER);
+            wait_slow(bars + 8 * (C::B_KV_FULL + slot), ph, drain_flag, 100000000ull, C::B_KV_FULL + slot,
+                      ROLE_PRODUCER);
         }
       }
     }
     __syncwarp();
   } else if (warp == MMA_WARP) {
+    // ----------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC_QK = idesc_f16_f32(BM, BN, 0, 0);
       const int dpv = (p.D + 15) & ~15;  // PV N dimension (multiple of 16)
@@ -346,7 +446,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int ksteps = (p.D + 15) / 16;  // QK reduction steps over the head dim
       const uint32_t tS0 = tmem + 0, tS1 = tmem + 128;
       const uint32_t tO0 = tmem + 256, tO1 = tmem + 256 + DP;
-
       // Descriptors are built once; an MMA step only adds its byte offset >> 4
       // to the start-address field (all tiles lie below 256 KiB of shared
       // memory, so the field never carries into the next one).
@@ -368,53 +467,68 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                      (acc || k > 0) ? 1u : 0u);
       };
 
-      bool ok = bwait(bars, C::B_Q, 0, abort_flag, tmo, ROLE_MMA);
-      tc_fence_after();
-      int it = 0;
-      int prev_v_slot = 0;
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int k_slot = it % C::STAGES;
-        const uint32_t k_ph = (it / C::STAGES) & 1;
-        ++it;
-        const int v_slot = it % C::STAGES;
-        const uint32_t v_ph = (it / C::STAGES) & 1;
-        ++it;
-
-        if (!bwait(bars, C::B_KV_FULL + k_slot, k_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+      SegIter si;
+      si.init(p, cta, G);
+      int unit, t0, t1;
+      bool fs;
+      int it = 0, qseg = 0;
+      uint32_t g0 = 0, g1 = 0;  // S/P phases completed per query tile
+      bool ok = true;
+      while (ok && si.next(unit, t0, t1, fs)) {
+        const int bh = unit / p.n_qb;
+        const int q_row0 = (unit - bh * p.n_qb) * (2 * BM);
+        const bool has1 = (q_row0 + BM) < p.Sq;
+        if (!bwait(bars, C::B_Q_FULL, qseg & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+        ++qseg;
         tc_fence_after();
-        issue_qk(tS0, dQ0, k_slot * C::TILE_BYTES);  // S0(j); PV0(j-1) was issued before it
-        tc_commit(bars + 8 * (C::B_S_FULL + 0));
-        if (has1) {
-          if (j > 0) {
-            if (!bwait(bars, C::B_P_FULL + 1, (j - 1) & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
-            tc_fence_after();
-            issue_pv(tO1, tS1, prev_v_slot * C::TILE_BYTES, j - 1 > 0);
-            tc_commit(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));  // V(j-1) free
-          }
-          issue_qk(tS1, dQ1, k_slot * C::TILE_BYTES);
-          tc_commit(bars + 8 * (C::B_S_FULL + 1));
-        }
-        tc_commit(bars + 8 * (C::B_KV_EMPTY + k_slot));  // K(j) free
-        if (!bwait(bars, C::B_KV_FULL + v_slot, v_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
-        if (!bwait(bars, C::B_P_FULL + 0, j & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
-        tc_fence_after();
-        issue_pv(tO0, tS0, v_slot * C::TILE_BYTES, j > 0);
-        if (!has1) tc_commit(bars + 8 * (C::B_KV_EMPTY + v_slot));
-        prev_v_slot = v_slot;
-      }
-      if (ok && has1 && n_tiles > 0) {
-        if (bwait(bars, C::B_P_FULL + 1, (n_tiles - 1) & 1, abort_flag, tmo, ROLE_MMA)) {
+        int prev_v_slot = 0;
+        for (int j = t0; j < t1; ++j) {
+          const int k_slot = it % C::STAGES;
+          const uint32_t k_ph = (it / C::STAGES) & 1;
+          ++it;
+          const int v_slot = it % C::STAGES;
+          const uint32_t v_ph = (it / C::STAGES) & 1;
+          ++it;
+          if (!bwait(bars, C::B_KV_FULL + k_slot, k_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(tO1, tS1, prev_v_slot * C::TILE_BYTES, n_tiles - 1 > 0);
-          tc_commit(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));
-        } else {
-          ok = false;
+          issue_qk(tS0, dQ0, k_slot * C::TILE_BYTES);  // S0(j); PV0(j-1) was issued before it
+          tc_commit(bars + 8 * (C::B_S_FULL + 0));
+          if (has1) {
+            if (j > t0) {
+              if (!bwait(bars, C::B_P_FULL + 1, (g1 - 1) & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+              tc_fence_after();
+              issue_pv(tO1, tS1, prev_v_slot * C::TILE_BYTES, j - 1 > t0);
+              tc_commit(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));  // V(j-1) free
+            }
+            issue_qk(tS1, dQ1, k_slot * C::TILE_BYTES);
+            tc_commit(bars + 8 * (C::B_S_FULL + 1));
+            ++g1;
+          }
+          tc_commit(bars + 8 * (C::B_KV_EMPTY + k_slot));  // K(j) free
+          if (j + 1 == t1) tc_commit(bars + 8 * C::B_Q_EMPTY);  // last S of this segment issued
+          if (!bwait(bars, C::B_KV_FULL + v_slot, v_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+          if (!bwait(bars, C::B_P_FULL + 0, g0 & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(tO0, tS0, v_slot * C::TILE_BYTES, j > t0);
+          ++g0;
+          if (!has1) tc_commit(bars + 8 * (C::B_KV_EMPTY + v_slot));
+          prev_v_slot = v_slot;
+        }
+        if (ok && has1) {
+          if (bwait(bars, C::B_P_FULL + 1, (g1 - 1) & 1, abort_flag, tmo, ROLE_MMA)) {
+            tc_fence_after();
+            issue_pv(tO1, tS1, prev_v_slot * C::TILE_BYTES, t1 - 1 > t0);
+            tc_commit(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));
+          } else {
+            ok = false;
+          }
+        }
+        if (ok) {
+          tc_commit(bars + 8 * (C::B_O_FULL + 0));
+          if (has1) tc_commit(bars + 8 * (C::B_O_FULL + 1));
         }
       }
-      if (ok) {
-        tc_commit(bars + 8 * (C::B_O_FULL + 0));
-        if (has1) tc_commit(bars + 8 * (C::B_O_FULL + 1));
-      } else {
+      if (!ok) {
         // Drain every MMA issued so far before TMEM and shared memory are released.
         tc_commit(bars + 8 * C::B_DRAIN);
         wait_slow(bars + 8 * C::B_DRAIN, 0, drain_flag, 100000000ull, C::B_DRAIN, ROLE_MMA);
@@ -428,17 +542,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int quad = warp & 3; // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const int role = ti ? ROLE_SOFTMAX1 : ROLE_SOFTMAX0;
-    if (ti == 0 || has1) {
-      const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-      const uint32_t tS = tmem + lane_off + ti * 128;
-      const uint32_t tO = tmem + lane_off + 256 + ti * DP;
-      const float sl2 = p.scale_log2;
-      const bool pos = sl2 >= 0.f;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t tS = tmem + lane_off + ti * 128;
+    const uint32_t tO = tmem + lane_off + 256 + ti * DP;
+    const float sl2 = p.scale_log2;
+    const bool pos = sl2 >= 0.f;
+    SegIter si;
+    si.init(p, cta, G);
+    int unit, t0, t1;
+    bool first_seg;
+    uint32_t g = 0, oseg = 0, wsync = 0;
+    bool ok = true;
+    auto wg_sync = [&]() -> bool {
+      mbar_arrive(bars + 8 * (C::B_WG + ti));
+      const bool r = bwait_warp(bars, C::B_WG + ti, wsync & 1, abort_flag, tmo, role);
+      ++wsync;
+      return r;
+    };
+    while (ok && si.next(unit, t0, t1, first_seg)) {
+      const int bh = unit / p.n_qb;
+      const int q_row0 = (unit - bh * p.n_qb) * (2 * BM);
+      const bool has1 = (q_row0 + BM) < p.Sq;
+      if (ti == 1 && !has1) continue;
       float m_run = -INFINITY;  // running max, already multiplied by scale*log2(e)
       float l_run = 0.f;
-      bool ok = true;
-      for (int j = 0; j < n_tiles; ++j) {
-        if (!bwait_warp(bars, C::B_S_FULL + ti, j & 1, abort_flag, tmo, role)) { ok = false; break; }
+      for (int j = t0; j < t1; ++j) {
+        if (!bwait_warp(bars, C::B_S_FULL + ti, g & 1, abort_flag, tmo, role)) { ok = false; break; }
         tc_fence_after();
         uint32_t s[BN];
 #pragma unroll
@@ -449,8 +578,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
         const int nvalid = min(BN, p.Skv - j * BN);
         const bool full = nvalid == BN;
-        // Row extreme of the raw scores: max for scale >= 0, min for scale < 0,
-        // so that extreme * scale is the max of the scaled scores.
         const float mx = row_extreme(s, nvalid, full, pos);
         const float m_cand = mx * sl2;
         const float m_new = fmaxf(m_run, m_cand);
@@ -462,8 +589,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         l_run *= factor;
         const float neg_m = -m_run;
-        // P = exp2(s * scale*log2(e) - m) as fp16 into the first 64 columns of
-        // S, written in two halves so that half of s[] is dead before the rest.
         float lsum0, lsum1;
         if (full)
           row_exp_store<false>(s, sl2, neg_m, nvalid, tS, lsum0, lsum1);
@@ -473,7 +598,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // Rescale this warp's O rows when any of them moved its max. PV(j-1)
         // of this tile completed before S(j) was signalled, and PV(j) is only
         // issued after this warpgroup arrives on P_FULL below.
-        if (j > 0 && __any_sync(0xffffffffu, need)) {
+        if (j > t0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll
           for (int c = 0; c < DP / 32; ++c) {
             uint32_t o[32];
@@ -488,44 +613,127 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(bars + 8 * (C::B_P_FULL + ti));
+        ++g;
       }
-      // ---------------------------------------------------------- epilogue
-      const bool have_o =
-          ok && n_tiles > 0 && bwait_warp(bars, C::B_O_FULL + ti, 0, abort_flag, tmo, role);
-      const uint32_t stage = ti ? sQ1 : sQ0;  // Q_i is dead: its last MMA completed
-      if (have_o) {
-        tc_fence_after();
+      if (!ok) break;
+      // -------------------------------------------------- segment epilogue
+      if (!bwait_warp(bars, C::B_O_FULL + ti, oseg & 1, abort_flag, tmo, role)) { ok = false; break; }
+      ++oseg;
+      tc_fence_after();
+      const int q_row = q_row0 + ti * BM + row;
+      const bool live = q_row < p.Sq;
+      __half* orow = p.o + (static_cast<long long>(bh) * p.Sq + (live ? q_row : 0)) * p.D;
+      if (t0 == 0 && t1 == p.n_tiles) {
+        // whole unit: O / l straight to global memory
         const float inv = 1.f / l_run;
 #pragma unroll
-        for (int c = 0; c < C::NCHUNK; ++c) {
-          uint32_t o[64];
-          tmem_ld32(tO + 64 * c, o);
-          tmem_ld32(tO + 64 * c + 32, o + 32);
+        for (int c = 0; c < DP / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + 32 * c, o);
           tmem_wait_ld();
           reg_fence32(o);
-          reg_fence32(o + 32);
-          const uint32_t rowbase = stage + c * CHUNK_BYTES + row * 128;
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const uint32_t a = pack_half2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
-            const uint32_t b = pack_half2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
-            const uint32_t cc = pack_half2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
-            const uint32_t d = pack_half2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
-            st_shared_v4(rowbase + ((u ^ (row & 7)) << 4), a, b, cc, d);
-          }
+          if (live) store_row_f16(orow, c * 32, p.D, o, inv);
         }
-        fence_proxy_async_smem();
+        continue;
       }
-      // Every thread of the warpgroup arrives (written or not); one thread
-      // waits, bounded, for all 128 rows before storing the tile.
-      mbar_arrive(bars + 8 * (C::B_EPI + ti));
-      if (quad == 0 && lane == 0 && have_o &&
-          bwait(bars, C::B_EPI + ti, 0, abort_flag, tmo, role)) {
+      // partial piece: unnormalised O, m and l to this CTA's workspace slot
+      const int which = first_seg ? 0 : 1;
+      const long long slot = (static_cast<long long>(cta) * 2 + which) * 2 + ti;
+      float* wo = p.ws_o + (slot * BM + row) * DP;
+      float* wml = p.ws_ml + (slot * BM + row) * 2;
 #pragma unroll
-        for (int c = 0; c < C::NCHUNK; ++c)
-          tma_store_3d(&tm_o, stage + c * CHUNK_BYTES, c * 64, q_row0 + ti * BM, bh);
-        tma_store_commit();
-        tma_store_wait_read0();
+      for (int c = 0; c < DP / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + 32 * c, o);
+        tmem_wait_ld();
+        reg_fence32(o);
+        float4* dst = reinterpret_cast<float4*>(wo + c * 32);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          dst[e] = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+                               __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
+      }
+      *reinterpret_cast<float2*>(wml) = make_float2(m_run, l_run);
+      __threadfence();
+      if (!wg_sync()) { ok = false; break; }
+      unsigned long long* cnt = p.ws_cnt + unit * 2 + ti;
+      const long long W = p.total_steps;
+      const long long ubase = static_cast<long long>(unit) * p.n_tiles;
+      const int c_lo = owner_cta(ubase, W, G);
+      const int c_hi = owner_cta(ubase + p.n_tiles - 1, W, G);
+      if (quad == 0 && lane == 0) {
+        // A counter whose tag is not this launch's epoch counts as 0, so the
+        // workspace needs no clearing between calls of any size.
+        unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(cnt), next;
+        while (true) {
+          next = (((cur >> 8) == p.epoch) ? cur : (p.epoch << 8)) + 1ull;
+          const unsigned long long seen = atomicCAS(cnt, cur, next);
+          if (seen == cur) break;
+          cur = seen;
+        }
+        last_flag[ti] = (static_cast<int>(next & 0xffull) == c_hi - c_lo + 1) ? 1 : 0;
+      }
+      if (!wg_sync()) { ok = false; break; }
+      if (last_flag[ti]) {
+        // last piece to finish: combine every piece of this unit's tile, in
+        // CTA order whoever combines, so that the result is deterministic
+        __threadfence();
+        float m_all = -INFINITY;
+        for (int c2 = c_lo; c2 <= c_hi; ++c2) {
+          float m2 = m_run;
+          if (c2 != cta) {
+            const int which2 = (range_begin(W, G, c2) / p.n_tiles == unit) ? 0 : 1;
+            const long long slot2 = (static_cast<long long>(c2) * 2 + which2) * 2 + ti;
+            m2 = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot2 * BM + row) * 2)).x;
+          }
+          m_all = fmaxf(m_all, m2);
+        }
+        float l_all = 0.f;
+        for (int c2 = c_lo; c2 <= c_hi; ++c2) {
+          float2 ml = make_float2(m_run, l_run);
+          if (c2 != cta) {
+            const int which2 = (range_begin(W, G, c2) / p.n_tiles == unit) ? 0 : 1;
+            const long long slot2 = (static_cast<long long>(c2) * 2 + which2) * 2 + ti;
+            ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot2 * BM + row) * 2));
+          }
+          l_all = fmaf(ml.y, ex2_approx(ml.x - m_all), l_all);
+        }
+        const float inv = 1.f / l_all;
+#pragma unroll 1
+        for (int c = 0; c < DP / 32; ++c) {
+          uint32_t own[32];
+          tmem_ld32(tO + 32 * c, own);
+          tmem_wait_ld();
+          reg_fence32(own);
+          float acc[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+          for (int c2 = c_lo; c2 <= c_hi; ++c2) {
+            if (c2 == cta) {
+              const float w = ex2_approx(m_run - m_all);
+#pragma unroll
+              for (int e = 0; e < 32; ++e) acc[e] = fmaf(__uint_as_float(own[e]), w, acc[e]);
+            } else {
+              const int which2 = (range_begin(W, G, c2) / p.n_tiles == unit) ? 0 : 1;
+              const long long slot2 = (static_cast<long long>(c2) * 2 + which2) * 2 + ti;
+              const float w = ex2_approx(
+                  __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot2 * BM + row) * 2)).x - m_all);
+              const float4* src = reinterpret_cast<const float4*>(p.ws_o + (slot2 * BM + row) * DP + c * 32);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float4 v4 = __ldcg(src + e);
+                acc[4 * e] = fmaf(v4.x, w, acc[4 * e]);
+                acc[4 * e + 1] = fmaf(v4.y, w, acc[4 * e + 1]);
+                acc[4 * e + 2] = fmaf(v4.z, w, acc[4 * e + 2]);
+                acc[4 * e + 3] = fmaf(v4.w, w, acc[4 * e + 3]);
+              }
+            }
+          }
+          uint32_t o[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(acc[e]);
+          if (live) store_row_f16(orow, c * 32, p.D, o, inv);
+        }
       }
     }
   }
@@ -882,6 +1090,7 @@ struct DeviceInfo {
   bool checked = false;
   bool sm100 = false;
   bool attrs_set = false;
+  int num_sms = 0;
 };
 constexpr int kMaxDevices = 64;
 DeviceInfo g_dev[kMaxDevices];
@@ -899,6 +1108,8 @@ int check_device(int* dev_out) {
         cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
       return GFX906_B200_ECUDA;
     di.sm100 = (major == 10 && minor == 0);
+    if (cudaDeviceGetAttribute(&di.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return GFX906_B200_ECUDA;
     di.checked = true;
   }
   if (!di.sm100) return GFX906_B200_ENODEV;
@@ -916,6 +1127,8 @@ int check_device(int* dev_out) {
   return GFX906_B200_OK;
 }
 
+int device_sms(int dev) { return g_dev[dev].num_sms > 0 ? g_dev[dev].num_sms : 1; }
+
 unsigned long long timeout_ns_from_env() {
   static unsigned long long v = [] {
     const char* e = getenv("GFX906_B200_WAIT_TIMEOUT_MS");
@@ -926,28 +1139,92 @@ unsigned long long timeout_ns_from_env() {
   return v;
 }
 
+// Launch epochs tag the split counters (56 bits: never reused in practice).
+std::atomic<unsigned long long> g_epoch{1};
+unsigned long long next_epoch() { return g_epoch.fetch_add(1) & ((1ull << 56) - 1); }
+
+// Persistent schedule of attn_fwd_kernel (see SegIter in the kernel).
+struct Plan {
+  int G = 0;      // CTAs (at most one per SM)
+  int split = 0;  // stream-K split of the key range across CTAs
+  int n_qb = 0, n_units = 0, n_tiles = 0;
+  long long total_steps = 0;
+};
+constexpr int kMinSplitSteps = 4;   // shortest key range a CTA gets when splitting
+constexpr int kMinSplitTiles = 16;  // units shorter than this are never split
+
+bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Plan* pl) {
+  pl->n_qb = (Sq + 2 * fa::BM - 1) / (2 * fa::BM);
+  pl->n_tiles = (Skv + fa::BN - 1) / fa::BN;
+  const long long U = static_cast<long long>(pl->n_qb) * BH;
+  if (U > 0x7fffffffll) return false;
+  pl->n_units = static_cast<int>(U);
+  pl->total_steps = U * pl->n_tiles;
+  const long long G = num_sms;
+  // Split the key range across CTAs only where whole units would leave many SMs
+  // idle (fewer units than SMs, or a last wave that wastes over a quarter of
+  // the machine) and units are long enough to amortise the combine (>= 16 key
+  // tiles). Measured on B200: 16384 x 131072 x D64 on one head, 64 units:
+  // 267 -> 593 TFLOP/s; B2 H16 Sq4096 Skv1024 D128 (8 key tiles): split loses.
+  const long long waves = (U + G - 1) / G;
+  const double idle = 1.0 - static_cast<double>(U) / static_cast<double>(waves * G);
+  // Long units (>= 64 key tiles) amortise the combine well enough to split at
+  // a smaller loss (1 x 32768 x 32768 x D64, 128 units: 522 -> 579 TFLOP/s).
+  const bool worth = idle > 0.25 || (idle > 0.10 && pl->n_tiles >= 64);
+  pl->split = (allow_split && pl->n_tiles >= kMinSplitTiles && worth) ? 1 : 0;
+  long long g = pl->split ? (pl->total_steps + kMinSplitSteps - 1) / kMinSplitSteps : U;
+  if (g > G) g = G;
+  if (g < 1) g = 1;
+  pl->G = static_cast<int>(g);
+  return true;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Workspace of a split plan: [counters][partial (m, l)][partial O].
+size_t workspace_bytes(const Plan& pl, int DP) {
+  if (!pl.split) return 0;
+  const size_t slots = static_cast<size_t>(pl.G) * 2 * 2 * fa::BM;
+  return align256(static_cast<size_t>(pl.n_units) * 2 * sizeof(unsigned long long)) +
+         align256(slots * 2 * sizeof(float)) + slots * DP * sizeof(float);
+}
+
 template <int DP>
-int launch_dp(const void* q, const void* k, const void* v, void* o, long long BH, int Sq, int Skv,
-              int D, float scale, cudaStream_t stream) {
-  CUtensorMap mq, mk, mv, mo;
+int launch_dp(const void* q, const void* k, const void* v, void* o, long long BH, int Sq, int Skv, int D,
+              float scale, void* ws, size_t ws_size, int dev, cudaStream_t stream) {
+  Plan pl;
+  if (!make_plan(BH, Sq, Skv, device_sms(dev), ws != nullptr, &pl)) return GFX906_B200_EINVAL;
+  CUtensorMap mq, mk, mv;
   if (!make_map(&mq, q, D, Sq, BH, fa::BM) || !make_map(&mk, k, D, Skv, BH, fa::BN) ||
-      !make_map(&mv, v, D, Skv, BH, fa::BN) || !make_map(&mo, o, D, Sq, BH, fa::BM))
+      !make_map(&mv, v, D, Skv, BH, fa::BN))
     return GFX906_B200_ECUDA;
-  fa::Params prm;
+  fa::Params prm{};
   prm.Sq = Sq;
   prm.Skv = Skv;
   prm.D = D;
+  prm.bh_offset = 0;
   prm.scale_log2 = scale * 1.4426950408889634f;
   prm.timeout_ns = timeout_ns_from_env();
-  const unsigned qblocks = static_cast<unsigned>((Sq + 2 * fa::BM - 1) / (2 * fa::BM));
-  for (long long off = 0; off < BH; off += 65535) {
-    const long long n = (BH - off) < 65535 ? (BH - off) : 65535;
-    prm.bh_offset = static_cast<int>(off);
-    dim3 grid(qblocks, static_cast<unsigned>(n), 1);
-    fa::attn_fwd_kernel<DP><<<grid, fa::NUM_THREADS, fa::Cfg<DP>::SMEM_BYTES, stream>>>(mq, mk, mv, mo, prm);
-    if (cudaGetLastError() != cudaSuccess) return GFX906_B200_ECUDA;
+  prm.n_qb = pl.n_qb;
+  prm.n_units = pl.n_units;
+  prm.n_tiles = pl.n_tiles;
+  prm.split = pl.split;
+  prm.total_steps = pl.total_steps;
+  prm.o = static_cast<__half*>(o);
+  if (pl.split) {
+    const size_t need = workspace_bytes(pl, DP);
+    if (ws_size < need || (reinterpret_cast<uintptr_t>(ws) & 255u)) return GFX906_B200_EINVAL;
+    uint8_t* base = static_cast<uint8_t*>(ws);
+    const size_t slots = static_cast<size_t>(pl.G) * 2 * 2 * fa::BM;
+    prm.ws_cnt = reinterpret_cast<unsigned long long*>(base);
+    base += align256(static_cast<size_t>(pl.n_units) * 2 * sizeof(unsigned long long));
+    prm.epoch = next_epoch();
+    prm.ws_ml = reinterpret_cast<float*>(base);
+    base += align256(slots * 2 * sizeof(float));
+    prm.ws_o = reinterpret_cast<float*>(base);
   }
-  return GFX906_B200_OK;
+  fa::attn_fwd_kernel<DP><<<pl.G, fa::NUM_THREADS, fa::Cfg<DP>::SMEM_BYTES, stream>>>(mq, mk, mv, prm);
+  return cudaGetLastError() == cudaSuccess ? GFX906_B200_OK : GFX906_B200_ECUDA;
 }
 
 int launch_d512(const void* q, const void* k, const void* v, void* o, long long BH, int Sq, int Skv,
@@ -956,7 +1233,7 @@ int launch_d512(const void* q, const void* k, const void* v, void* o, long long 
   if (!make_map(&mq, q, 512, Sq, BH, fa::BM) || !make_map(&mk, k, 512, Skv, BH, fa::BN) ||
       !make_map(&mv, v, 512, Skv, BH, fa::BN) || !make_map(&mo, o, 512, Sq, BH, fa::BM))
     return GFX906_B200_ECUDA;
-  fa::Params prm;
+  fa::Params prm{};
   prm.Sq = Sq;
   prm.Skv = Skv;
   prm.D = 512;
@@ -973,12 +1250,18 @@ int launch_d512(const void* q, const void* k, const void* v, void* o, long long 
   return GFX906_B200_OK;
 }
 
-int attn_launch_impl(const void* q, const void* k, const void* v, void* o, int B, int H, int Sq, int Skv,
-                     int D, float scale, cudaStream_t stream) {
+// Argument checks shared by every entry point. Returns OK and sets *skip when
+// there is nothing to compute.
+int check_args(const void* q, const void* k, const void* v, const void* o, int B, int H, int Sq, int Skv,
+               int D, bool* skip) {
+  *skip = false;
   if (B < 0 || H < 0 || Sq < 0 || Skv < 0) return GFX906_B200_EINVAL;
   if (!((D >= 8 && D <= 64 && D % 8 == 0) || D == 128 || D == 512)) return GFX906_B200_EHEADDIM;
   const long long BH = static_cast<long long>(B) * H;
-  if (BH == 0 || Sq == 0) return GFX906_B200_OK;
+  if (BH == 0 || Sq == 0) {
+    *skip = true;
+    return GFX906_B200_OK;
+  }
   if (BH > (1ll << 31) || static_cast<long long>(Sq) * D * 2 * BH >= (1ll << 40) ||
       static_cast<long long>(Skv) * D * 2 * BH >= (1ll << 40))
     return GFX906_B200_EINVAL;
@@ -987,8 +1270,17 @@ int attn_launch_impl(const void* q, const void* k, const void* v, void* o, int B
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
        reinterpret_cast<uintptr_t>(o)) & 15u)
     return GFX906_B200_EALIGN;
+  return GFX906_B200_OK;
+}
+
+int attn_launch_impl(const void* q, const void* k, const void* v, void* o, int B, int H, int Sq, int Skv,
+                     int D, float scale, void* ws, size_t ws_size, cudaStream_t stream) {
+  bool skip = false;
+  int rc = check_args(q, k, v, o, B, H, Sq, Skv, D, &skip);
+  if (rc != GFX906_B200_OK || skip) return rc;
+  const long long BH = static_cast<long long>(B) * H;
   int dev = 0;
-  int rc = check_device(&dev);
+  rc = check_device(&dev);
   if (rc != GFX906_B200_OK) return rc;
   if (Skv == 0) {
     // softmax over an empty key set: defined here as a zero output.
@@ -996,8 +1288,8 @@ int attn_launch_impl(const void* q, const void* k, const void* v, void* o, int B
       return GFX906_B200_ECUDA;
     return GFX906_B200_OK;
   }
-  if (D == 128) return launch_dp<128>(q, k, v, o, BH, Sq, Skv, D, scale, stream);
-  if (D <= 64) return launch_dp<64>(q, k, v, o, BH, Sq, Skv, D, scale, stream);
+  if (D == 128) return launch_dp<128>(q, k, v, o, BH, Sq, Skv, D, scale, ws, ws_size, dev, stream);
+  if (D <= 64) return launch_dp<64>(q, k, v, o, BH, Sq, Skv, D, scale, ws, ws_size, dev, stream);
   return launch_d512(q, k, v, o, BH, Sq, Skv, scale, stream);
 }
 
@@ -1007,7 +1299,28 @@ extern "C" {
 
 int gfx906_b200_attn_launch(const void* q, const void* k, const void* v, void* o, int B, int H, int Sq,
                             int Skv, int D, float scale, cudaStream_t stream) {
-  const int rc = attn_launch_impl(q, k, v, o, B, H, Sq, Skv, D, scale, stream);
+  const int rc = attn_launch_impl(q, k, v, o, B, H, Sq, Skv, D, scale, nullptr, 0, stream);
+  t_last_error = rc;
+  return rc;
+}
+
+size_t gfx906_b200_attn_workspace_size(int B, int H, int Sq, int Skv, int D) {
+  bool skip = false;
+  const int probe = 16;  // any aligned non-null value: only sizes are checked here
+  const void* fake = reinterpret_cast<const void*>(static_cast<uintptr_t>(probe));
+  if (check_args(fake, fake, fake, fake, B, H, Sq, Skv, D, &skip) != GFX906_B200_OK || skip) return 0;
+  if (Skv == 0 || D == 512) return 0;
+  int dev = 0;
+  if (check_device(&dev) != GFX906_B200_OK) return 0;
+  Plan pl;
+  if (!make_plan(static_cast<long long>(B) * H, Sq, Skv, device_sms(dev), true, &pl)) return 0;
+  return workspace_bytes(pl, D == 128 ? 128 : 64);
+}
+
+int gfx906_b200_attn_launch_ws(const void* q, const void* k, const void* v, void* o, int B, int H, int Sq,
+                               int Skv, int D, float scale, void* workspace, size_t workspace_bytes,
+                               cudaStream_t stream) {
+  const int rc = attn_launch_impl(q, k, v, o, B, H, Sq, Skv, D, scale, workspace, workspace_bytes, stream);
   t_last_error = rc;
   return rc;
 }

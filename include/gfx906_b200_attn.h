@@ -20,6 +20,7 @@
 #ifndef GFX906_B200_ATTN_H
 #define GFX906_B200_ATTN_H
 
+#include <stddef.h>
 #include <cuda_runtime_api.h>
 
 #if defined(__GNUC__)
@@ -54,6 +55,26 @@ GFX906_B200_API void launch(const void* q, const void* k, const void* v, void* o
 GFX906_B200_API int gfx906_b200_attn_launch(const void* q, const void* k, const void* v,
                             void* o, int B, int H, int Sq, int Skv, int D,
                             float scale, cudaStream_t stream);
+
+/* Bytes of workspace gfx906_b200_attn_launch_ws needs for these sizes on the
+ * current device (0 when the call does not split work across CTAs). No
+ * reference counterpart: the reference's kernels keep nothing between CTAs. */
+GFX906_B200_API size_t gfx906_b200_attn_workspace_size(int B, int H, int Sq, int Skv, int D);
+
+/* Same work as gfx906_b200_attn_launch, with a caller-owned device workspace
+ * that lets the kernel balance the key range of every (batch, head, query
+ * block) across all SMs (partial results are combined on the GPU). The
+ * workspace must be 256-byte aligned and at least
+ * gfx906_b200_attn_workspace_size() bytes; its contents on entry do not
+ * matter (arrival counters are tagged with a per-launch epoch), so it needs
+ * no clearing and may be reused for calls of any size. Calls that share a
+ * workspace must not overlap on the GPU (use one stream, or one workspace per
+ * stream). Extension of attn_kernel.hip:710-742 (same arguments plus the
+ * workspace). */
+GFX906_B200_API int gfx906_b200_attn_launch_ws(const void* q, const void* k, const void* v,
+                               void* o, int B, int H, int Sq, int Skv, int D,
+                               float scale, void* workspace, size_t workspace_bytes,
+                               cudaStream_t stream);
 
 /* Status of the last launch()/gfx906_b200_attn_launch() on this host thread.
  * No reference counterpart (the reference's launch returns void). */
