@@ -68,12 +68,13 @@ def test_workspace_size_and_checks(lib):
     assert lib.workspace_size(1, 4, 1024, 1024, 512) == 0  # D=512 never splits
     assert lib.workspace_size(1, 4, 1024, 0, 64) == 0
     assert lib.workspace_size(1, 4, 1024, 1024, 100) == 0
-    n = lib.workspace_size(1, 24, 4096, 4096, 128)
+    assert lib.workspace_size(1, 24, 4096, 4096, 128) == 0  # whole units leave few SMs idle
+    n = lib.workspace_size(1, 24, 2000, 3000, 128)  # 192 units on 148 SMs: split
     assert n > 0
-    q, k, v = make_qkv(1, 24, 4096, 4096, 128, device="cuda")
+    q, k, v = make_qkv(1, 24, 2000, 3000, 128, device="cuda")
     o = torch.empty_like(q)
     small = torch.zeros(256, dtype=torch.uint8, device="cuda")
-    rc = lib.launch_ws_status(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 1, 24, 4096, 4096, 128,
+    rc = lib.launch_ws_status(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 1, 24, 2000, 3000, 128,
                               0.1, small.data_ptr(), 256, torch.cuda.current_stream().cuda_stream)
     assert rc == STATUS["EINVAL"]
     assert lib.device_status(reset=False) == STATUS["OK"]
