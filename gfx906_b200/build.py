@@ -36,7 +36,7 @@ EXT_NAME = "_attn_ext"
 EXT_PATH = PKG_DIR / (EXT_NAME + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 
 # Every CUDA translation unit of the library.
-CU_SOURCES = [CSRC / "attn_fwd_sm100.cu"]
+CU_SOURCES = [CSRC / "attn_fwd_sm100.cu", CSRC / "attn_fwd_noalloc.cu"]
 CU_HEADERS = [CSRC / "sm100_ptx.cuh", INCLUDE / "gfx906_b200_attn.h"]
 
 NVCC_FLAGS = [

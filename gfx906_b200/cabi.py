@@ -10,7 +10,8 @@ from __future__ import annotations
 import ctypes
 from pathlib import Path
 
-STATUS = {"OK": 0, "EINVAL": 1, "EHEADDIM": 2, "EALIGN": 3, "ENODEV": 4, "ECUDA": 5, "ETIMEOUT": 6}
+STATUS = {"OK": 0, "EINVAL": 1, "EHEADDIM": 2, "EALIGN": 3, "ENODEV": 4, "ECUDA": 5, "ETIMEOUT": 6,
+          "ENOSPACE": 7}
 
 _c_int, _c_void_p, _c_float = ctypes.c_int, ctypes.c_void_p, ctypes.c_float
 
@@ -38,6 +39,10 @@ class CABI:
         d.gfx906_b200_attn_workspace_size.restype = ctypes.c_size_t
         d.gfx906_b200_attn_launch_ws.argtypes = sig[:-1] + [_c_void_p, ctypes.c_size_t, _c_void_p]
         d.gfx906_b200_attn_launch_ws.restype = _c_int
+        d.gfx906_b200_attn_launch_noalloc.argtypes = sig
+        d.gfx906_b200_attn_launch_noalloc.restype = _c_int
+        d.gfx906_b200_attn_noalloc_capacity.argtypes = []
+        d.gfx906_b200_attn_noalloc_capacity.restype = ctypes.c_size_t
         d.gfx906_b200_attn_flops.argtypes = [_c_int] * 5
         d.gfx906_b200_attn_flops.restype = ctypes.c_double
 
@@ -47,6 +52,9 @@ class CABI:
     def launch_ws_status(self, q, k, v, o, B, H, Sq, Skv, D, scale, ws, ws_bytes, stream=None) -> int:
         return self.dll.gfx906_b200_attn_launch_ws(q, k, v, o, B, H, Sq, Skv, D, _c_float(scale), ws,
                                                    ws_bytes, stream)
+
+    def launch_noalloc_status(self, q, k, v, o, B, H, Sq, Skv, D, scale, stream=None) -> int:
+        return self.dll.gfx906_b200_attn_launch_noalloc(q, k, v, o, B, H, Sq, Skv, D, _c_float(scale), stream)
 
     def workspace_size(self, B, H, Sq, Skv, D) -> int:
         return self.dll.gfx906_b200_attn_workspace_size(B, H, Sq, Skv, D)

@@ -1341,6 +1341,7 @@ const char* gfx906_b200_attn_error_string(int status) {
     case GFX906_B200_ENODEV: return "current CUDA device is not an sm_100 (B200) GPU";
     case GFX906_B200_ECUDA: return "a CUDA runtime or driver call failed";
     case GFX906_B200_ETIMEOUT: return "a kernel wait timed out (device status word set)";
+    case GFX906_B200_ENOSPACE: return "the call needs more scratch than the allocation-free entry point's array holds";
     default: return "unknown status";
   }
 }

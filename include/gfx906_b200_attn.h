@@ -41,6 +41,7 @@ extern "C" {
 #define GFX906_B200_ENODEV 4      /* current device is not sm_100 */
 #define GFX906_B200_ECUDA 5       /* a CUDA runtime or driver call failed */
 #define GFX906_B200_ETIMEOUT 6    /* a kernel wait ran out (device status word) */
+#define GFX906_B200_ENOSPACE 7    /* needs more scratch than the built-in array holds */
 
 /* Replaces attn_kernel.hip:710-742 `launch` (same arguments; cudaStream_t for
  * hipStream_t). Returns nothing, like the reference; the status of the call
@@ -75,6 +76,25 @@ GFX906_B200_API int gfx906_b200_attn_launch_ws(const void* q, const void* k, con
                                void* o, int B, int H, int Sq, int Skv, int D,
                                float scale, void* workspace, size_t workspace_bytes,
                                cudaStream_t stream);
+
+/* Allocation-free form of gfx906_b200_attn_launch_ws, for callers that cannot
+ * allocate device memory (a plugin whose host runtime owns all device memory,
+ * an application with a fixed memory budget, a latency-critical path where
+ * cudaMalloc/cudaFree would lock or synchronise). Its scratch is a fixed
+ * array of gfx906_b200_attn_noalloc_capacity() bytes (48 MiB) compiled into
+ * the library; a GPU holds it from the first call on that device until the
+ * process exits. That first call looks up the array's device address and
+ * should come before any stream capture on the device. Calls whose split
+ * schedule needs more scratch return GFX906_B200_ENOSPACE. All calls on a
+ * device share the array: calls that overlap on the GPU race, so order them
+ * on one stream. Allocates nothing. No counterpart in the reference. */
+GFX906_B200_API int gfx906_b200_attn_launch_noalloc(const void* q, const void* k, const void* v,
+                                    void* o, int B, int H, int Sq, int Skv, int D,
+                                    float scale, cudaStream_t stream);
+
+/* Size in bytes of the scratch array behind gfx906_b200_attn_launch_noalloc.
+ * No counterpart in the reference. */
+GFX906_B200_API size_t gfx906_b200_attn_noalloc_capacity(void);
 
 /* Status of the last launch()/gfx906_b200_attn_launch() on this host thread.
  * No reference counterpart (the reference's launch returns void). */
