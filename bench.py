@@ -59,6 +59,9 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--shard", default="heads", choices=["heads", "rows"],
+                    help="heads: every rank its own batch of (batch x head) units (weak scaling); "
+                         "rows: one problem, query rows split over ranks, K/V broadcast (strong scaling)")
     return ap.parse_args()
 
 
@@ -240,6 +243,67 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_rows(args, rank, world, local):
+    """Strong scaling of one problem: query rows split over ranks, K/V replicated
+    from rank 0 by NCCL broadcast (gfx906_b200.shard.attention_by_rows)."""
+    import gfx906_b200
+    from gfx906_b200 import shard
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if gfx906_b200.load_attention() is None:
+        raise RuntimeError(f"sm_100 attention operator unavailable: {gfx906_b200.last_error()}")
+    cfg = CONFIGS[args.config]
+    q, k, v = make_qkv(cfg.B, cfg.H, cfg.Sq, cfg.Skv, cfg.D, cfg.seed, cfg.std)
+    sh = shard.row_shard(cfg.Sq, rank, world)
+    q_rows = q[:, :, sh.start:sh.stop].contiguous().to(dev)
+    kd, vd = k.to(dev), v.to(dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(3, args.warmup)):
+        gfx906_b200.attn(q_rows, kd, vd, cfg.scale)
+    torch.cuda.synchronize()
+    # kernel only, max over ranks
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    with sampler:
+        e0.record(stream)
+        for _ in range(args.steps):
+            gfx906_b200.attn(q_rows, kd, vd, cfg.scale)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    # broadcast + kernel + all-gather, max over ranks
+    steps_sh = max(1, min(args.steps, 10))
+    barrier(world)
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(steps_sh):
+        shard.attention_by_rows(q_rows, kd, vd, cfg.scale, cfg.Sq, src=0)
+    e3.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms_sh = max_over_ranks(e2.elapsed_time(e3), world)
+    if rank != 0:
+        return
+    value = cfg.flops * args.steps / (ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"{cfg.name}: {cfg.describe()}",
+                   "parallelism": f"query rows split over {world} GPU(s) in 256-row blocks, K/V broadcast"},
+        "sharded_e2e": {"value": cfg.flops * steps_sh / (ms_sh * 1e-3) / 1e12, "unit": UNIT,
+                        "ms_per_step": ms_sh / steps_sh,
+                        "includes": "NCCL broadcast of K and V, kernel, all-gather of O"},
+        "clocks": sampler.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, rank, world, local):
     import gfx906_b200
 
@@ -405,6 +469,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.shard == "rows":
+            run_rows(args, rank, world, local)
         else:
             run_ours(args, rank, world, local)
     finally:

@@ -1,0 +1,130 @@
+"""Multi-GPU partitioning of the attention forward (one process per GPU).
+
+The path partitions without any exchange on the data path: every
+(batch, head, query-row block) is independent given its K and V. Two layouts,
+as the north star of this build describes them:
+
+* ``"heads"``: the B*H (batch x head) units are cut into contiguous blocks,
+  one per rank; each rank holds and computes only its own units.
+* ``"rows"``: for few heads with very long sequences (e.g. B=1, H=1,
+  S=131072), the query rows are cut into contiguous blocks of whole 256-row
+  kernel query blocks, one per rank, and K/V -- held by one source rank -- are
+  replicated to every rank with one NCCL broadcast each before the kernel runs.
+
+Optionally the output blocks are all-gathered. Collectives happen only before
+and after the local kernel call (``torch.distributed`` over NCCL on GPUs; the
+same code runs over gloo on CPU in the tests). The local compute is
+``gfx906_b200.attn`` (the sm_100a kernel); tests inject a CPU stand-in.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+ROW_ALIGN = 256  # query rows per kernel CTA unit: row shards stay whole units
+
+
+@dataclass(frozen=True)
+class Shard:
+    """A contiguous [start, stop) block of units (heads or query rows)."""
+
+    start: int
+    stop: int
+
+    @property
+    def size(self) -> int:
+        return self.stop - self.start
+
+
+def split_even(n: int, world: int, rank: int, align: int = 1) -> Shard:
+    """Rank's block of n items cut into `world` near-equal blocks of whole `align` groups."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    groups = (n + align - 1) // align
+    lo = groups * rank // world
+    hi = groups * (rank + 1) // world
+    return Shard(min(n, lo * align), min(n, hi * align))
+
+
+def head_shard(B: int, H: int, rank: int, world: int) -> Shard:
+    """Rank's block of the flattened (batch x head) index b * H + h."""
+    return split_even(B * H, world, rank)
+
+
+def row_shard(Sq: int, rank: int, world: int) -> Shard:
+    """Rank's block of query rows, in whole 256-row kernel units."""
+    return split_even(Sq, world, rank, ROW_ALIGN)
+
+
+def _default_attn():
+    import gfx906_b200
+
+    return gfx906_b200.attn
+
+
+def _group_world(group):
+    if not dist.is_available() or not dist.is_initialized():
+        return 1, 0  # a single process: no collectives
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def _gather_dim(local: torch.Tensor, counts, dim: int, group) -> torch.Tensor:
+    """All-gather blocks of unequal size along `dim` (padded to the largest)."""
+    world = len(counts)
+    biggest = max(counts)
+    pad = list(local.shape)
+    pad[dim] = biggest
+    buf = local.new_zeros(pad)
+    buf.narrow(dim, 0, local.shape[dim]).copy_(local)
+    parts = [torch.empty_like(buf) for _ in range(world)]
+    dist.all_gather(parts, buf, group=group)
+    return torch.cat([p.narrow(dim, 0, c) for p, c in zip(parts, counts)], dim=dim)
+
+
+def attention_by_heads(q, k, v, scale, group=None, gather=True,
+                       local_attn: Optional[Callable] = None):
+    """Each rank computes its block of (batch x head) units; q/k/v are full
+    [B,H,S,D] tensors present on every rank (only the rank's slice is read).
+    Returns the full output if `gather`, else this rank's [units, Sq, D] block."""
+    attn = local_attn or _default_attn()
+    world, rank = _group_world(group)
+    B, H, Sq, D = q.shape
+    sh = head_shard(B, H, rank, world)
+    qf = q.reshape(B * H, Sq, D)[sh.start:sh.stop]
+    kf = k.reshape(B * H, k.shape[2], D)[sh.start:sh.stop]
+    vf = v.reshape(B * H, v.shape[2], D)[sh.start:sh.stop]
+    out = attn(qf.unsqueeze(0), kf.unsqueeze(0), vf.unsqueeze(0), scale).squeeze(0)
+    if not gather:
+        return out
+    if world == 1:
+        return out.reshape(B, H, Sq, D)
+    counts = [head_shard(B, H, r, world).size for r in range(world)]
+    return _gather_dim(out, counts, 0, group).reshape(B, H, Sq, D)
+
+
+def attention_by_rows(q_rows, k, v, scale, Sq: int, src: int = 0, group=None, gather=True,
+                      local_attn: Optional[Callable] = None):
+    """Query-row sharding with K/V replicated from rank `src`.
+
+    q_rows: this rank's query rows [B, H, rows, D] (its `row_shard` of Sq).
+    k, v: full [B, H, Skv, D] on rank `src`; on other ranks tensors of the
+    same shape and dtype that receive the broadcast.
+    Returns the full [B, H, Sq, D] output if `gather`, else this rank's rows.
+    """
+    attn = local_attn or _default_attn()
+    world, rank = _group_world(group)
+    sh = row_shard(Sq, rank, world)
+    if q_rows.shape[2] != sh.size:
+        raise ValueError(f"rank {rank} holds {q_rows.shape[2]} query rows, its shard is {sh.size}")
+    if world > 1:
+        dist.broadcast(k, src=src, group=group)
+        dist.broadcast(v, src=src, group=group)
+    out = attn(q_rows, k, v, scale) if sh.size > 0 else q_rows.new_zeros(q_rows.shape)
+    if not gather or world == 1:
+        return out
+    counts = [row_shard(Sq, r, world).size for r in range(world)]
+    return _gather_dim(out, counts, 2, group)

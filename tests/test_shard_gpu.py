@@ -1,0 +1,70 @@
+"""Sharded attention over NCCL on 2+ GPUs of one box (skipped with fewer GPUs).
+
+Each rank runs the sm_100a kernel on its shard; the gathered result must equal
+a single-GPU call on the full problem (same kernel, same rows: identical bits
+for the row layout, whose per-row work does not depend on the shard).
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, result_q):
+    import datetime
+
+    import gfx906_b200
+    from gfx906_b200 import shard
+    from gfx906_b200.configs import make_qkv
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        errs = []
+        # rows: one head, long sequence, K/V only on rank 0
+        Sq, Skv, D = 4096 + 300, 8192, 64
+        q, k, v = make_qkv(1, 1, Sq, Skv, D, seed=3)
+        sh = shard.row_shard(Sq, rank, world)
+        q_rows = q[:, :, sh.start:sh.stop].contiguous().cuda()
+        kd, vd = (k.cuda(), v.cuda()) if rank == 0 else (torch.zeros_like(k).cuda(), torch.zeros_like(v).cuda())
+        out = shard.attention_by_rows(q_rows, kd, vd, D ** -0.5, Sq, src=0)
+        full = gfx906_b200.attn(q.cuda(), k.cuda(), v.cuda(), D ** -0.5)
+        errs.append(float((out.float() - full.float()).abs().max()))
+        # heads: (batch x head) blocks
+        q, k, v = make_qkv(2, 5, 1000, 777, 128, seed=4)
+        out = shard.attention_by_heads(q.cuda(), k.cuda(), v.cuda(), 128 ** -0.5)
+        full = gfx906_b200.attn(q.cuda(), k.cuda(), v.cuda(), 128 ** -0.5)
+        errs.append(float((out.float() - full.float()).abs().max()))
+        torch.cuda.synchronize()
+        if rank == 0:
+            result_q.put(errs)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_attention_nccl():
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs 2 or more GPUs")
+    world = min(n, 4)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    mp.start_processes(_worker, args=(world, _free_port(), q), nprocs=world, start_method="spawn", join=True)
+    errs = q.get(timeout=120)
+    assert errs[0] <= 2e-3 and errs[1] <= 2e-3, errs
