@@ -91,12 +91,14 @@ struct Params {
   int n_qb;               // 256-row query blocks per (batch, head)
   int n_units;            // n_qb * B * H
   int n_tiles;            // 128-key tiles per unit
-  int split;              // 1: stream-K split of the key range; 0: whole units
-  long long total_steps;  // n_units * n_tiles
+  int split;              // 1: whole units, then a stream-K split of the tail units
+  int tail_unit0;         // first unit of the split tail (split mode)
+  int tail_ctas;          // CTAs that share the tail's key range (split mode)
+  long long total_steps;  // (n_units - tail_unit0) * n_tiles: steps of the tail
   __half* o;              // output, [B*H, Sq, D] fp16
-  float* ws_o;            // split workspace: [G][2][2][128][DP] partial O
-  float* ws_ml;           // [G][2][2][128][2] partial (m, l)
-  unsigned long long* ws_cnt;  // [n_units][2] arrival counters: (epoch << 8) | arrivals
+  float* ws_o;            // split workspace: [tail_ctas][2][2][128][DP] partial O
+  float* ws_ml;           // [tail_ctas][2][2][128][2] partial (m, l)
+  unsigned long long* ws_cnt;  // [tail units][2] arrival counters: (epoch << 8) | arrivals
   unsigned long long epoch;    // unique per launch (56 bits), tags the counters
 };
 
@@ -267,46 +269,50 @@ __device__ __forceinline__ void row_exp_store(const uint32_t* s, float sl2, floa
 
 // Persistent schedule shared by every role of attn_fwd_kernel: a CTA walks a
 // list of segments (unit, first key tile, end key tile). A unit is one
-// 256-row query block of one (batch, head). In split mode CTA c owns the
-// contiguous range [c*W/G, (c+1)*W/G) of the W = units * key-tiles steps, so
-// work is balanced to one key tile; a unit whose key range spans several CTAs
-// is computed as partial pieces that are combined by the last one to finish.
-// In whole mode CTA c takes units c, c+G, c+2G, ... (no partials).
+// 256-row query block of one (batch, head). CTA c first takes whole units c,
+// c+G, c+2G, ... below tail_unit0 (all units in whole mode). In split mode the
+// remaining "tail" units are then shared by the first tail_ctas CTAs: CTA c
+// owns the contiguous range [c*W/tail_ctas, (c+1)*W/tail_ctas) of the tail's
+// W = units * key-tiles steps, so the machine stays balanced to one key tile;
+// a tail unit whose key range spans several CTAs is computed as partial
+// pieces, combined by the last one to finish. Partials only ever occur at the
+// end of a CTA's work.
 struct SegIter {
   long long s, s_end;
-  int u, u_step, T, U;
-  bool split, first;
-  __device__ __forceinline__ void init(const Params& p, int c, int G) {
-    split = p.split != 0;
+  int u, G, T, tail0;
+  bool first_tail;
+  __device__ __forceinline__ void init(const Params& p, int c, int G_) {
+    G = G_;
     T = p.n_tiles;
-    U = p.n_units;
-    first = true;
-    if (split) {
-      s = static_cast<long long>(c) * p.total_steps / G;
-      s_end = static_cast<long long>(c + 1) * p.total_steps / G;
-    } else {
-      u = c;
-      u_step = G;
+    u = c;
+    tail0 = p.split ? p.tail_unit0 : p.n_units;
+    s = s_end = 0;
+    if (p.split && c < p.tail_ctas) {
+      s = static_cast<long long>(c) * p.total_steps / p.tail_ctas;
+      s_end = static_cast<long long>(c + 1) * p.total_steps / p.tail_ctas;
     }
+    first_tail = true;
   }
+  // first_seg: this is the CTA's first tail segment (selects its partial slot).
   __device__ __forceinline__ bool next(int& unit, int& t0, int& t1, bool& first_seg) {
-    if (split) {
-      if (s >= s_end) return false;
-      unit = static_cast<int>(s / T);
-      const long long ubase = static_cast<long long>(unit) * T;
-      const long long e = (s_end < ubase + T) ? s_end : ubase + T;
-      t0 = static_cast<int>(s - ubase);
-      t1 = static_cast<int>(e - ubase);
-      s = e;
-    } else {
-      if (u >= U) return false;
+    if (u < tail0) {
       unit = u;
       t0 = 0;
       t1 = T;
-      u += u_step;
+      u += G;
+      first_seg = false;
+      return true;
     }
-    first_seg = first;
-    first = false;
+    if (s >= s_end) return false;
+    const int rel = static_cast<int>(s / T);
+    unit = tail0 + rel;
+    const long long ubase = static_cast<long long>(rel) * T;
+    const long long e = (s_end < ubase + T) ? s_end : ubase + T;
+    t0 = static_cast<int>(s - ubase);
+    t1 = static_cast<int>(e - ubase);
+    s = e;
+    first_seg = first_tail;
+    first_tail = false;
     return true;
   }
 };
@@ -656,11 +662,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       *reinterpret_cast<float2*>(wml) = make_float2(m_run, l_run);
       __threadfence();
       if (!wg_sync()) { ok = false; break; }
-      unsigned long long* cnt = p.ws_cnt + unit * 2 + ti;
+      const int rel = unit - p.tail_unit0;  // index of the unit within the split tail
+      unsigned long long* cnt = p.ws_cnt + rel * 2 + ti;
       const long long W = p.total_steps;
-      const long long ubase = static_cast<long long>(unit) * p.n_tiles;
-      const int c_lo = owner_cta(ubase, W, G);
-      const int c_hi = owner_cta(ubase + p.n_tiles - 1, W, G);
+      const int GT = p.tail_ctas;
+      const long long ubase = static_cast<long long>(rel) * p.n_tiles;
+      const int c_lo = owner_cta(ubase, W, GT);
+      const int c_hi = owner_cta(ubase + p.n_tiles - 1, W, GT);
       if (quad == 0 && lane == 0) {
         // A counter whose tag is not this launch's epoch counts as 0, so the
         // workspace needs no clearing between calls of any size.
@@ -682,7 +690,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int c2 = c_lo; c2 <= c_hi; ++c2) {
           float m2 = m_run;
           if (c2 != cta) {
-            const int which2 = (range_begin(W, G, c2) / p.n_tiles == unit) ? 0 : 1;
+            const int which2 = (range_begin(W, GT, c2) / p.n_tiles == rel) ? 0 : 1;
             const long long slot2 = (static_cast<long long>(c2) * 2 + which2) * 2 + ti;
             m2 = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot2 * BM + row) * 2)).x;
           }
@@ -692,7 +700,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int c2 = c_lo; c2 <= c_hi; ++c2) {
           float2 ml = make_float2(m_run, l_run);
           if (c2 != cta) {
-            const int which2 = (range_begin(W, G, c2) / p.n_tiles == unit) ? 0 : 1;
+            const int which2 = (range_begin(W, GT, c2) / p.n_tiles == rel) ? 0 : 1;
             const long long slot2 = (static_cast<long long>(c2) * 2 + which2) * 2 + ti;
             ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot2 * BM + row) * 2));
           }
@@ -714,7 +722,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
               for (int e = 0; e < 32; ++e) acc[e] = fmaf(__uint_as_float(own[e]), w, acc[e]);
             } else {
-              const int which2 = (range_begin(W, G, c2) / p.n_tiles == unit) ? 0 : 1;
+              const int which2 = (range_begin(W, GT, c2) / p.n_tiles == rel) ? 0 : 1;
               const long long slot2 = (static_cast<long long>(c2) * 2 + which2) * 2 + ti;
               const float w = ex2_approx(
                   __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot2 * BM + row) * 2)).x - m_all);
@@ -1145,13 +1153,16 @@ unsigned long long next_epoch() { return g_epoch.fetch_add(1) & ((1ull << 56) - 
 
 // Persistent schedule of attn_fwd_kernel (see SegIter in the kernel).
 struct Plan {
-  int G = 0;      // CTAs (at most one per SM)
-  int split = 0;  // stream-K split of the key range across CTAs
+  int G = 0;          // CTAs (at most one per SM)
+  int split = 0;      // whole units, then a stream-K split of the tail units
+  int tail_unit0 = 0;
+  int tail_ctas = 0;
   int n_qb = 0, n_units = 0, n_tiles = 0;
-  long long total_steps = 0;
+  long long total_steps = 0;  // steps of the tail
 };
-constexpr int kMinSplitSteps = 4;   // shortest key range a CTA gets when splitting
-constexpr int kMinSplitTiles = 16;  // units shorter than this are never split
+constexpr int kMinSplitSteps = 4;   // shortest key range a CTA gets in the tail
+constexpr int kMinSplitTiles = 16;      // fewer units than SMs: split units of >= 16 key tiles
+constexpr int kMinSplitTilesTail = 64;  // a partial last wave: split units of >= 64 key tiles
 
 bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Plan* pl) {
   pl->n_qb = (Sq + 2 * fa::BM - 1) / (2 * fa::BM);
@@ -1159,23 +1170,31 @@ bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Pla
   const long long U = static_cast<long long>(pl->n_qb) * BH;
   if (U > 0x7fffffffll) return false;
   pl->n_units = static_cast<int>(U);
-  pl->total_steps = U * pl->n_tiles;
   const long long G = num_sms;
-  // Split the key range across CTAs only where whole units would leave many SMs
-  // idle (fewer units than SMs, or a last wave that wastes over a quarter of
-  // the machine) and units are long enough to amortise the combine (>= 16 key
-  // tiles). Measured on B200: 16384 x 131072 x D64 on one head, 64 units:
-  // 267 -> 593 TFLOP/s; B2 H16 Sq4096 Skv1024 D128 (8 key tiles): split loses.
-  const long long waves = (U + G - 1) / G;
-  const double idle = 1.0 - static_cast<double>(U) / static_cast<double>(waves * G);
-  // Long units (>= 64 key tiles) amortise the combine well enough to split at
-  // a smaller loss (1 x 32768 x 32768 x D64, 128 units: 522 -> 579 TFLOP/s).
-  const bool worth = idle > 0.25 || (idle > 0.10 && pl->n_tiles >= 64);
-  pl->split = (allow_split && pl->n_tiles >= kMinSplitTiles && worth) ? 1 : 0;
-  long long g = pl->split ? (pl->total_steps + kMinSplitSteps - 1) / kMinSplitSteps : U;
-  if (g > G) g = G;
-  if (g < 1) g = 1;
-  pl->G = static_cast<int>(g);
+  const long long waves = U / G;       // full waves of whole units
+  const long long tail = U - waves * G;  // units left for a partial last wave
+  // Split the tail's key range over the CTAs when whole units would leave SMs
+  // idle in the last wave and units are long enough to amortise writing and
+  // combining partial results: >= 16 key tiles when there are fewer units than
+  // SMs, >= 64 otherwise. Measured on B200 (TFLOP/s, whole -> split):
+  // 1x16384x131072 D64 (64 units) 275 -> 614; 1x131072^2 D64 (512 units,
+  // 1024 key tiles) 544 -> 634; B1 H24 S4096 D128 (32 key tiles) 950 -> 908.
+  const bool long_units = pl->n_tiles >= (waves == 0 ? kMinSplitTiles : kMinSplitTilesTail);
+  pl->split = (allow_split && tail > 0 && long_units) ? 1 : 0;
+  if (pl->split) {
+    pl->tail_unit0 = static_cast<int>(waves * G);
+    pl->total_steps = tail * pl->n_tiles;
+    long long gt = (pl->total_steps + kMinSplitSteps - 1) / kMinSplitSteps;
+    if (gt > G) gt = G;
+    pl->tail_ctas = static_cast<int>(gt);
+    pl->G = static_cast<int>(waves > 0 ? G : gt);
+  } else {
+    pl->tail_unit0 = pl->n_units;
+    pl->tail_ctas = 0;
+    pl->total_steps = 0;
+    pl->G = static_cast<int>(U < G ? U : G);
+    if (pl->G < 1) pl->G = 1;
+  }
   return true;
 }
 
@@ -1184,8 +1203,8 @@ size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 // Workspace of a split plan: [counters][partial (m, l)][partial O].
 size_t workspace_bytes(const Plan& pl, int DP) {
   if (!pl.split) return 0;
-  const size_t slots = static_cast<size_t>(pl.G) * 2 * 2 * fa::BM;
-  return align256(static_cast<size_t>(pl.n_units) * 2 * sizeof(unsigned long long)) +
+  const size_t slots = static_cast<size_t>(pl.tail_ctas) * 2 * 2 * fa::BM;
+  return align256(static_cast<size_t>(pl.n_units - pl.tail_unit0) * 2 * sizeof(unsigned long long)) +
          align256(slots * 2 * sizeof(float)) + slots * DP * sizeof(float);
 }
 
@@ -1209,15 +1228,17 @@ int launch_dp(const void* q, const void* k, const void* v, void* o, long long BH
   prm.n_units = pl.n_units;
   prm.n_tiles = pl.n_tiles;
   prm.split = pl.split;
+  prm.tail_unit0 = pl.tail_unit0;
+  prm.tail_ctas = pl.tail_ctas;
   prm.total_steps = pl.total_steps;
   prm.o = static_cast<__half*>(o);
   if (pl.split) {
     const size_t need = workspace_bytes(pl, DP);
     if (ws_size < need || (reinterpret_cast<uintptr_t>(ws) & 255u)) return GFX906_B200_EINVAL;
     uint8_t* base = static_cast<uint8_t*>(ws);
-    const size_t slots = static_cast<size_t>(pl.G) * 2 * 2 * fa::BM;
+    const size_t slots = static_cast<size_t>(pl.tail_ctas) * 2 * 2 * fa::BM;
     prm.ws_cnt = reinterpret_cast<unsigned long long*>(base);
-    base += align256(static_cast<size_t>(pl.n_units) * 2 * sizeof(unsigned long long));
+    base += align256(static_cast<size_t>(pl.n_units - pl.tail_unit0) * 2 * sizeof(unsigned long long));
     prm.epoch = next_epoch();
     prm.ws_ml = reinterpret_cast<float*>(base);
     base += align256(slots * 2 * sizeof(float));

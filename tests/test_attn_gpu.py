@@ -172,7 +172,10 @@ def test_long_sequence_memory_is_linear(op):
     out = op.attn(q, k, v, 0.125)
     torch.cuda.synchronize()
     peak = torch.cuda.max_memory_allocated() - base
-    assert peak <= out.numel() * 2 + (1 << 20), peak
+    # the output plus the split workspace, whose size depends on the SM count
+    # and head dim, not on S (at most 48 MiB on a B200); S*S fp32 scores alone
+    # would be 8 * 32768^2 * 4 B = 32 GiB
+    assert peak <= out.numel() * 2 + (48 << 20), peak
     rows = sample_rows(S, n_each=64, seed=14)
     check_rows(out.cpu(), q.cpu(), k.cpu(), v.cpu(), 0.125, rows, what="S=32768")
 
