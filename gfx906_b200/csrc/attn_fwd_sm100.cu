@@ -15,7 +15,7 @@
 //    L2 once per 256 query rows.
 //  * A producer warp streams Q (once) and K/V tiles (in a ring of shared-memory
 //    stages) with TMA, 128-byte swizzled, completion tracked by mbarriers.
-//  * One thread of the MMA warp issues every tcgen05.mma: S_i = Q_i K^T
+//  * The MMA warp issues every tcgen05.mma (one elected lane): S_i = Q_i K^T
 //    (fp16 x fp16 -> fp32, both operands from shared memory) into tensor memory
 //    (TMEM), and O_i += P_i V with P_i read from TMEM and V from shared memory.
 //  * Two softmax warpgroups (one per query tile, one thread per query row =
@@ -445,7 +445,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncwarp();
   } else if (warp == MMA_WARP) {
     // ----------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the issue loop with identical values (so descriptors
+    // stay in uniform registers); elect.sync picks the lane that issues each
+    // tcgen05.mma / tcgen05.commit.
+    {
       constexpr uint32_t IDESC_QK = idesc_f16_f32(BM, BN, 0, 0);
       const int dpv = (p.D + 15) & ~15;  // PV N dimension (multiple of 16)
       const uint32_t idesc_pv = idesc_f16_f32(BM, dpv, 0, 1);
@@ -463,13 +466,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int k = 0; k < DP / 16; ++k) {
           const uint32_t off = static_cast<uint32_t>((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4;
           if (DP == 128 || k < ksteps)
-            mma_f16_ss(d_tmem, dq + off, dK + ((kv_off >> 4) + off), IDESC_QK, k > 0 ? 1u : 0u);
+            mma_f16_ss_warp(d_tmem, dq + off, dK + ((kv_off >> 4) + off), IDESC_QK, k > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](uint32_t d_tmem, uint32_t p_tmem, uint32_t v_off, bool acc) {
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k)
-          mma_f16_ts(d_tmem, p_tmem + 8 * k, dV + ((v_off + k * 2048) >> 4), idesc_pv,
+          mma_f16_ts_warp(d_tmem, p_tmem + 8 * k, dV + ((v_off + k * 2048) >> 4), idesc_pv,
                      (acc || k > 0) ? 1u : 0u);
       };
 
@@ -484,7 +487,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int bh = unit / p.n_qb;
         const int q_row0 = (unit - bh * p.n_qb) * (2 * BM);
         const bool has1 = (q_row0 + BM) < p.Sq;
-        if (!bwait(bars, C::B_Q_FULL, qseg & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+        if (!bwait_warp(bars, C::B_Q_FULL, qseg & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
         ++qseg;
         tc_fence_after();
         int prev_v_slot = 0;
@@ -495,48 +498,48 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int v_slot = it % C::STAGES;
           const uint32_t v_ph = (it / C::STAGES) & 1;
           ++it;
-          if (!bwait(bars, C::B_KV_FULL + k_slot, k_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+          if (!bwait_warp(bars, C::B_KV_FULL + k_slot, k_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
           tc_fence_after();
           issue_qk(tS0, dQ0, k_slot * C::TILE_BYTES);  // S0(j); PV0(j-1) was issued before it
-          tc_commit(bars + 8 * (C::B_S_FULL + 0));
+          tc_commit_warp(bars + 8 * (C::B_S_FULL + 0));
           if (has1) {
             if (j > t0) {
-              if (!bwait(bars, C::B_P_FULL + 1, (g1 - 1) & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+              if (!bwait_warp(bars, C::B_P_FULL + 1, (g1 - 1) & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
               tc_fence_after();
               issue_pv(tO1, tS1, prev_v_slot * C::TILE_BYTES, j - 1 > t0);
-              tc_commit(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));  // V(j-1) free
+              tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));  // V(j-1) free
             }
             issue_qk(tS1, dQ1, k_slot * C::TILE_BYTES);
-            tc_commit(bars + 8 * (C::B_S_FULL + 1));
+            tc_commit_warp(bars + 8 * (C::B_S_FULL + 1));
             ++g1;
           }
-          tc_commit(bars + 8 * (C::B_KV_EMPTY + k_slot));  // K(j) free
-          if (j + 1 == t1) tc_commit(bars + 8 * C::B_Q_EMPTY);  // last S of this segment issued
-          if (!bwait(bars, C::B_KV_FULL + v_slot, v_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
-          if (!bwait(bars, C::B_P_FULL + 0, g0 & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+          tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + k_slot));  // K(j) free
+          if (j + 1 == t1) tc_commit_warp(bars + 8 * C::B_Q_EMPTY);  // last S of this segment issued
+          if (!bwait_warp(bars, C::B_KV_FULL + v_slot, v_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+          if (!bwait_warp(bars, C::B_P_FULL + 0, g0 & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
           tc_fence_after();
           issue_pv(tO0, tS0, v_slot * C::TILE_BYTES, j > t0);
           ++g0;
-          if (!has1) tc_commit(bars + 8 * (C::B_KV_EMPTY + v_slot));
+          if (!has1) tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + v_slot));
           prev_v_slot = v_slot;
         }
         if (ok && has1) {
-          if (bwait(bars, C::B_P_FULL + 1, (g1 - 1) & 1, abort_flag, tmo, ROLE_MMA)) {
+          if (bwait_warp(bars, C::B_P_FULL + 1, (g1 - 1) & 1, abort_flag, tmo, ROLE_MMA)) {
             tc_fence_after();
             issue_pv(tO1, tS1, prev_v_slot * C::TILE_BYTES, t1 - 1 > t0);
-            tc_commit(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));
+            tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));
           } else {
             ok = false;
           }
         }
         if (ok) {
-          tc_commit(bars + 8 * (C::B_O_FULL + 0));
-          if (has1) tc_commit(bars + 8 * (C::B_O_FULL + 1));
+          tc_commit_warp(bars + 8 * (C::B_O_FULL + 0));
+          if (has1) tc_commit_warp(bars + 8 * (C::B_O_FULL + 1));
         }
       }
       if (!ok) {
         // Drain every MMA issued so far before TMEM and shared memory are released.
-        tc_commit(bars + 8 * C::B_DRAIN);
+        tc_commit_warp(bars + 8 * C::B_DRAIN);
         wait_slow(bars + 8 * C::B_DRAIN, 0, drain_flag, 100000000ull, C::B_DRAIN, ROLE_MMA);
       }
     }
@@ -877,7 +880,8 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
     __syncwarp();
   } else if (warp == 5) {
     // ----------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // Whole-warp issue loop, one elected lane per tcgen05 instruction.
+    {
       constexpr uint32_t IDESC_QK = idesc_f16_f32(BM, BN, 0, 0);
       constexpr uint32_t IDESC_PV = idesc_f16_f32(BM, 128, 0, 1);
       const uint64_t dQ = sdesc_sw128(sQ, 16, 1024);
@@ -885,13 +889,13 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
       const uint64_t dV = sdesc_sw128(sRing, CHUNK_BYTES, 1024);
       const uint32_t tO = tmem + 256;
       int it = 0;
-      bool ok = bwait(bars, C::B_Q, 0, abort_flag, tmo, ROLE_MMA);
+      bool ok = bwait_warp(bars, C::B_Q, 0, abort_flag, tmo, ROLE_MMA);
       tc_fence_after();
       auto next_slot = [&](int& slot) -> bool {
         slot = it % C::SLOTS;
         const uint32_t ph = (it / C::SLOTS) & 1;
         ++it;
-        if (!bwait(bars, C::B_KV_FULL + slot, ph, abort_flag, tmo, ROLE_MMA)) return false;
+        if (!bwait_warp(bars, C::B_KV_FULL + slot, ph, abort_flag, tmo, ROLE_MMA)) return false;
         tc_fence_after();
         return true;
       };
@@ -905,15 +909,15 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
           for (int k = 0; k < 8; ++k) {
             const uint32_t qoff = static_cast<uint32_t>((2 * s + (k >> 2)) * CHUNK_BYTES + (k & 3) * 32) >> 4;
             const uint32_t koff = soff + (static_cast<uint32_t>((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4);
-            mma_f16_ss(tS, dQ + qoff, dK + koff, IDESC_QK, (s > 0 || k > 0) ? 1u : 0u);
+            mma_f16_ss_warp(tS, dQ + qoff, dK + koff, IDESC_QK, (s > 0 || k > 0) ? 1u : 0u);
           }
-          tc_commit(bars + 8 * (C::B_KV_EMPTY + slot));
+          tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + slot));
         }
-        tc_commit(bars + 8 * (C::B_S_FULL + (j & 1)));
+        tc_commit_warp(bars + 8 * (C::B_S_FULL + (j & 1)));
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
-        if (!bwait(bars, C::B_P_FULL + (j & 1), (j >> 1) & 1, abort_flag, tmo, ROLE_MMA)) return false;
+        if (!bwait_warp(bars, C::B_P_FULL + (j & 1), (j >> 1) & 1, abort_flag, tmo, ROLE_MMA)) return false;
         tc_fence_after();
         const uint32_t tP = tmem + 128 * (j & 1);
         for (int s = 0; s < 2; ++s) {
@@ -922,11 +926,11 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
           const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
 #pragma unroll
           for (int k = 0; k < BN / 16; ++k)
-            mma_f16_ts(tO + 128 * s, tP + 8 * k, dV + soff + ((k * 2048) >> 4), IDESC_PV,
+            mma_f16_ts_warp(tO + 128 * s, tP + 8 * k, dV + soff + ((k * 2048) >> 4), IDESC_PV,
                        (j > 0 || k > 0) ? 1u : 0u);
-          tc_commit(bars + 8 * (C::B_KV_EMPTY + slot));
+          tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + slot));
         }
-        tc_commit(bars + 8 * C::B_PV_DONE);
+        tc_commit_warp(bars + 8 * C::B_PV_DONE);
         return true;
       };
       for (int j = 0; j <= n_tiles && ok; ++j) {
@@ -934,9 +938,9 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
         if (ok && j > 0) ok = issue_pv(j - 1);
       }
       if (ok) {
-        tc_commit(bars + 8 * C::B_O_FULL);
+        tc_commit_warp(bars + 8 * C::B_O_FULL);
       } else {
-        tc_commit(bars + 8 * C::B_DRAIN);
+        tc_commit_warp(bars + 8 * C::B_DRAIN);
         wait_slow(bars + 8 * C::B_DRAIN, 0, drain_flag, 100000000ull, C::B_DRAIN, ROLE_MMA);
       }
     }
