@@ -384,7 +384,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp >= 8) setmaxnreg_dec<REGS_CONTROL>();  // whole control warpgroup, one instruction
   if (warp == PRODUCER_WARP) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    // Whole-warp loop; one elected lane issues each TMA and expect-tx.
+    {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
@@ -399,13 +400,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int q_row0 = (unit - bh * p.n_qb) * (2 * BM);
         const bool has1 = (q_row0 + BM) < p.Sq;
         // The Q buffers are free once every S MMA of the previous segment is done.
-        if (!bwait(bars, C::B_Q_EMPTY, (qseg & 1) ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) { ok = false; break; }
-        mbar_arrive_expect_tx(bars + 8 * C::B_Q_FULL, (has1 ? 2 : 1) * C::TILE_BYTES);
+        if (!bwait_warp(bars, C::B_Q_EMPTY, (qseg & 1) ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) { ok = false; break; }
+        mbar_arrive_expect_tx_warp(bars + 8 * C::B_Q_FULL, (has1 ? 2 : 1) * C::TILE_BYTES);
 #pragma unroll
         for (int c = 0; c < C::NCHUNK; ++c) {
-          tma_load_3d(sQ0 + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q_FULL, c * 64, q_row0, bh);
+          tma_load_3d_warp(sQ0 + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q_FULL, c * 64, q_row0, bh);
           if (has1)
-            tma_load_3d(sQ1 + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q_FULL, c * 64, q_row0 + BM, bh);
+            tma_load_3d_warp(sQ1 + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q_FULL, c * 64, q_row0 + BM, bh);
         }
         ++qseg;
         q_issued = 1;
@@ -414,16 +415,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int kv = 0; kv < 2; ++kv) {
             const int slot = it % C::STAGES;
             const uint32_t ph = (it / C::STAGES) & 1;
-            if (!bwait(bars, C::B_KV_EMPTY + slot, ph ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) {
+            if (!bwait_warp(bars, C::B_KV_EMPTY + slot, ph ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) {
               ok = false;
               break;
             }
             const uint32_t full = bars + 8 * (C::B_KV_FULL + slot);
-            mbar_arrive_expect_tx(full, C::TILE_BYTES);
+            mbar_arrive_expect_tx_warp(full, C::TILE_BYTES);
             const CUtensorMap* m = kv ? &tm_v : &tm_k;
 #pragma unroll
             for (int c = 0; c < C::NCHUNK; ++c)
-              tma_load_3d(sKV + slot * C::TILE_BYTES + c * CHUNK_BYTES, m, full, c * 64, j * BN, bh);
+              tma_load_3d_warp(sKV + slot * C::TILE_BYTES + c * CHUNK_BYTES, m, full, c * 64, j * BN, bh);
             ++it;
           }
         }
@@ -837,24 +838,25 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    // Whole-warp loop; one elected lane issues each TMA and expect-tx.
+    {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_o);
-      mbar_arrive_expect_tx(bars + 8 * C::B_Q, C::Q_BYTES);
-      for (int c = 0; c < 8; ++c) tma_load_3d(sQ + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q, c * 64, q_row0, bh);
+      mbar_arrive_expect_tx_warp(bars + 8 * C::B_Q, C::Q_BYTES);
+      for (int c = 0; c < 8; ++c) tma_load_3d_warp(sQ + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q, c * 64, q_row0, bh);
       int it = 0;
       bool ok = true;
       // slot order: K(0); then K(j), V(j-1) for j >= 1; then V(n-1)
       auto load_slot = [&](const CUtensorMap* m, int key0, int d0) -> bool {
         const int slot = it % C::SLOTS;
         const uint32_t ph = (it / C::SLOTS) & 1;
-        if (!bwait(bars, C::B_KV_EMPTY + slot, ph ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) return false;
+        if (!bwait_warp(bars, C::B_KV_EMPTY + slot, ph ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) return false;
         const uint32_t full = bars + 8 * (C::B_KV_FULL + slot);
-        mbar_arrive_expect_tx(full, C::SLOT_BYTES);
-        tma_load_3d(sRing + slot * C::SLOT_BYTES, m, full, d0, key0, bh);
-        tma_load_3d(sRing + slot * C::SLOT_BYTES + CHUNK_BYTES, m, full, d0 + 64, key0, bh);
+        mbar_arrive_expect_tx_warp(full, C::SLOT_BYTES);
+        tma_load_3d_warp(sRing + slot * C::SLOT_BYTES, m, full, d0, key0, bh);
+        tma_load_3d_warp(sRing + slot * C::SLOT_BYTES + CHUNK_BYTES, m, full, d0 + 64, key0, bh);
         ++it;
         return true;
       };
