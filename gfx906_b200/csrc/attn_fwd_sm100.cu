@@ -106,19 +106,23 @@ template <int DP>
 struct Cfg {
   static constexpr int NCHUNK = DP / 64;
   static constexpr int TILE_BYTES = NCHUNK * CHUNK_BYTES;
+  // Q buffers (2 lets the next unit's Q load during the current unit) and K/V
+  // stages. Measured on B200: at DP=128 a second Q buffer, which leaves room
+  // for only 3 stages, lost 2-5%; at DP=64 it made no difference.
+  static constexpr int QBUFS = 1;
   static constexpr int STAGES = (DP == 128) ? 4 : 8;
   // barrier indices
-  static constexpr int B_Q_FULL = 0;
-  static constexpr int B_Q_EMPTY = 1;
-  static constexpr int B_KV_FULL = 2;
-  static constexpr int B_KV_EMPTY = 2 + STAGES;
-  static constexpr int B_S_FULL = 2 + 2 * STAGES;
+  static constexpr int B_Q_FULL = 0;   // [2], per Q buffer
+  static constexpr int B_Q_EMPTY = 2;  // [2]
+  static constexpr int B_KV_FULL = 4;
+  static constexpr int B_KV_EMPTY = 4 + STAGES;
+  static constexpr int B_S_FULL = 4 + 2 * STAGES;
   static constexpr int B_P_FULL = B_S_FULL + 2;
   static constexpr int B_O_FULL = B_P_FULL + 2;
   static constexpr int B_WG = B_O_FULL + 2;  // per-warpgroup rendezvous, 2 barriers
   static constexpr int B_DRAIN = B_WG + 2;
   static constexpr int NUM_BARS = B_DRAIN + 1;
-  static constexpr int DATA_BYTES = (2 + STAGES) * TILE_BYTES;
+  static constexpr int DATA_BYTES = (2 * QBUFS + STAGES) * TILE_BYTES;
   static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + DATA_BYTES + NUM_BARS * 8 + 32;
 };
 
@@ -337,9 +341,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t s0 = (raw + 1023u) & ~1023u;  // 1024-B aligned for the 128B swizzle
   uint8_t* smem = smem_raw + (s0 - raw);
-  const uint32_t sQ0 = s0;
-  const uint32_t sQ1 = s0 + C::TILE_BYTES;
-  const uint32_t sKV = s0 + 2 * C::TILE_BYTES;
+  const uint32_t sQ = s0;  // Q buffer b, query tile i at sQ + (2 * b + i) * TILE_BYTES
+  const uint32_t sKV = s0 + 2 * C::QBUFS * C::TILE_BYTES;
   const uint32_t bars = s0 + C::DATA_BYTES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::DATA_BYTES + C::NUM_BARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -352,8 +355,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int cta = blockIdx.x;
 
   if (threadIdx.x == 0) {
-    mbar_init(bars + 8 * C::B_Q_FULL, 1);
-    mbar_init(bars + 8 * C::B_Q_EMPTY, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bars + 8 * (C::B_Q_FULL + b), 1);
+      mbar_init(bars + 8 * (C::B_Q_EMPTY + b), 1);
+    }
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bars + 8 * (C::B_KV_FULL + s), 1);
       mbar_init(bars + 8 * (C::B_KV_EMPTY + s), 1);
@@ -399,14 +404,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int bh = unit / p.n_qb;
         const int q_row0 = (unit - bh * p.n_qb) * (2 * BM);
         const bool has1 = (q_row0 + BM) < p.Sq;
-        // The Q buffers are free once every S MMA of the previous segment is done.
-        if (!bwait_warp(bars, C::B_Q_EMPTY, (qseg & 1) ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) { ok = false; break; }
-        mbar_arrive_expect_tx_warp(bars + 8 * C::B_Q_FULL, (has1 ? 2 : 1) * C::TILE_BYTES);
+        // Q buffer qb is free once every S MMA of the segment that last used
+        // it (QBUFS segments ago) is done.
+        const int qb = qseg % C::QBUFS;
+        const uint32_t qfull = bars + 8 * (C::B_Q_FULL + qb);
+        if (!bwait_warp(bars, C::B_Q_EMPTY + qb, ((qseg / C::QBUFS) & 1) ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx_warp(qfull, (has1 ? 2 : 1) * C::TILE_BYTES);
 #pragma unroll
         for (int c = 0; c < C::NCHUNK; ++c) {
-          tma_load_3d_warp(sQ0 + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q_FULL, c * 64, q_row0, bh);
+          tma_load_3d_warp(sQ + (2 * qb) * C::TILE_BYTES + c * CHUNK_BYTES, &tm_q, qfull, c * 64, q_row0, bh);
           if (has1)
-            tma_load_3d_warp(sQ1 + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q_FULL, c * 64, q_row0 + BM, bh);
+            tma_load_3d_warp(sQ + (2 * qb + 1) * C::TILE_BYTES + c * CHUNK_BYTES, &tm_q, qfull, c * 64,
+                             q_row0 + BM, bh);
         }
         ++qseg;
         q_issued = 1;
@@ -431,8 +443,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (!ok) {
         // Drain: every load issued must land before the CTA's shared memory goes away.
-        if (q_issued && !mbar_try_wait(bars + 8 * C::B_Q_FULL, (qseg - 1) & 1))
-          wait_slow(bars + 8 * C::B_Q_FULL, (qseg - 1) & 1, drain_flag, 100000000ull, C::B_Q_FULL, ROLE_PRODUCER);
+        // the last Q load into each buffer
+        for (int k = (qseg > C::QBUFS ? qseg - C::QBUFS : 0); q_issued && k < qseg; ++k) {
+          const uint32_t qf = bars + 8 * (C::B_Q_FULL + k % C::QBUFS);
+          if (!mbar_try_wait(qf, (k / C::QBUFS) & 1))
+            wait_slow(qf, (k / C::QBUFS) & 1, drain_flag, 100000000ull, C::B_Q_FULL + k % C::QBUFS,
+                      ROLE_PRODUCER);
+        }
         const int first = it > C::STAGES ? it - C::STAGES : 0;
         for (int t = first; t < it; ++t) {
           const int slot = t % C::STAGES;
@@ -459,7 +476,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // Descriptors are built once; an MMA step only adds its byte offset >> 4
       // to the start-address field (all tiles lie below 256 KiB of shared
       // memory, so the field never carries into the next one).
-      const uint64_t dQ0 = sdesc_sw128(sQ0, 16, 1024), dQ1 = sdesc_sw128(sQ1, 16, 1024);
+      const uint64_t dQ = sdesc_sw128(sQ, 16, 1024);
       const uint64_t dK = sdesc_sw128(sKV, 16, 1024);            // K-major K tiles
       const uint64_t dV = sdesc_sw128(sKV, CHUNK_BYTES, 1024);   // MN-major V tiles
       auto issue_qk = [&](uint32_t d_tmem, uint64_t dq, uint32_t kv_off) {
@@ -488,8 +505,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int bh = unit / p.n_qb;
         const int q_row0 = (unit - bh * p.n_qb) * (2 * BM);
         const bool has1 = (q_row0 + BM) < p.Sq;
-        if (!bwait_warp(bars, C::B_Q_FULL, qseg & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+        const int qb = qseg % C::QBUFS;
+        if (!bwait_warp(bars, C::B_Q_FULL + qb, (qseg / C::QBUFS) & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
         ++qseg;
+        const uint64_t dQ0 = dQ + ((2 * qb) * C::TILE_BYTES >> 4);
+        const uint64_t dQ1 = dQ + ((2 * qb + 1) * C::TILE_BYTES >> 4);
         tc_fence_after();
         int prev_v_slot = 0;
         for (int j = t0; j < t1; ++j) {
@@ -515,12 +535,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ++g1;
           }
           tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + k_slot));  // K(j) free
-          if (j + 1 == t1) tc_commit_warp(bars + 8 * C::B_Q_EMPTY);  // last S of this segment issued
+          if (j + 1 == t1) tc_commit_warp(bars + 8 * (C::B_Q_EMPTY + qb));  // last S of this segment issued
           if (!bwait_warp(bars, C::B_KV_FULL + v_slot, v_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
           if (!bwait_warp(bars, C::B_P_FULL + 0, g0 & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
           tc_fence_after();
           issue_pv(tO0, tS0, v_slot * C::TILE_BYTES, j > t0);
           ++g0;
+          if (j + 1 == t1) tc_commit_warp(bars + 8 * (C::B_O_FULL + 0));  // tile 0 epilogue may start
           if (!has1) tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + v_slot));
           prev_v_slot = v_slot;
         }
@@ -533,10 +554,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
           }
         }
-        if (ok) {
-          tc_commit_warp(bars + 8 * (C::B_O_FULL + 0));
-          if (has1) tc_commit_warp(bars + 8 * (C::B_O_FULL + 1));
-        }
+        if (ok && has1) tc_commit_warp(bars + 8 * (C::B_O_FULL + 1));
       }
       if (!ok) {
         // Drain every MMA issued so far before TMEM and shared memory are released.
