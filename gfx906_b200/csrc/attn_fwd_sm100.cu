@@ -65,6 +65,7 @@ constexpr uint32_t REGS_CONTROL = 96;
 constexpr int PRODUCER_WARP = 8;
 constexpr int MMA_WARP = 9;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+constexpr int MAX_PIECES = 4;              // most pieces one split unit is cut into
 #ifndef ATTN_EMU_PAIRS
 #define ATTN_EMU_PAIRS 1
 #endif
@@ -324,11 +325,14 @@ struct SegIter {
 __device__ __forceinline__ long long range_begin(long long W, int G, int c) {
   return static_cast<long long>(c) * W / G;
 }
-// Index of the CTA whose step range contains `step` (split mode).
+// Index of the CTA whose step range contains `step` (split mode). Range c
+// starts at floor(c * W / G), so "range c+1 starts at or before step" is
+// (c+1) * W < (step+1) * G: one division for the estimate, none to correct it.
 __device__ __forceinline__ int owner_cta(long long step, long long W, int G) {
   int c = static_cast<int>((step * G) / W);
-  while (c + 1 < G && range_begin(W, G, c + 1) <= step) ++c;
-  while (c > 0 && range_begin(W, G, c) > step) --c;
+  const long long lim = (step + 1) * G;
+  while (c + 1 < G && static_cast<long long>(c + 1) * W < lim) ++c;
+  while (c > 0 && static_cast<long long>(c) * W >= lim) --c;
   return c;
 }
 
@@ -682,7 +686,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
       }
       *reinterpret_cast<float2*>(wml) = make_float2(m_run, l_run);
-      __threadfence();
+      // Release: the warpgroup rendezvous orders every thread's stores before
+      // thread 0's gpu-scope fence, which orders them before the counter.
       if (!wg_sync()) { ok = false; break; }
       const int rel = unit - p.tail_unit0;  // index of the unit within the split tail
       unsigned long long* cnt = p.ws_cnt + rel * 2 + ti;
@@ -692,6 +697,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int c_lo = owner_cta(ubase, W, GT);
       const int c_hi = owner_cta(ubase + p.n_tiles - 1, W, GT);
       if (quad == 0 && lane == 0) {
+        __threadfence();
         // A counter whose tag is not this launch's epoch counts as 0, so the
         // workspace needs no clearing between calls of any size.
         unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(cnt), next;
@@ -701,61 +707,56 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (seen == cur) break;
           cur = seen;
         }
-        last_flag[ti] = (static_cast<int>(next & 0xffull) == c_hi - c_lo + 1) ? 1 : 0;
+        const int last = (static_cast<int>(next & 0xffull) == c_hi - c_lo + 1) ? 1 : 0;
+        if (last) __threadfence();  // acquire: the other pieces' stores are visible
+        last_flag[ti] = last;
       }
       if (!wg_sync()) { ok = false; break; }
       if (last_flag[ti]) {
-        // last piece to finish: combine every piece of this unit's tile, in
-        // CTA order whoever combines, so that the result is deterministic
-        __threadfence();
-        float m_all = -INFINITY;
-        for (int c2 = c_lo; c2 <= c_hi; ++c2) {
-          float m2 = m_run;
-          if (c2 != cta) {
-            const int which2 = (range_begin(W, GT, c2) / p.n_tiles == rel) ? 0 : 1;
-            const long long slot2 = (static_cast<long long>(c2) * 2 + which2) * 2 + ti;
-            m2 = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot2 * BM + row) * 2)).x;
-          }
-          m_all = fmaxf(m_all, m2);
+        // Last piece to finish: combine every piece of this (unit, query tile)
+        // from the workspace, in CTA order whoever combines (deterministic
+        // bits). One row per thread, all 128 rows in flight; per 32-column
+        // chunk the loads of every piece are issued together.
+        const int np = c_hi - c_lo + 1;  // <= MAX_PIECES (make_plan guarantees it)
+        long long rbase[MAX_PIECES];     // element offset of this row in each piece
+        float2 ml[MAX_PIECES];
+#pragma unroll
+        for (int k = 0; k < MAX_PIECES; ++k) {
+          const int c2 = c_lo + k;
+          // range c2 starts inside this unit (its first tail segment) iff
+          // floor(c2 * W / GT) >= ubase, i.e. c2 * W >= ubase * GT
+          const int which2 = (static_cast<long long>(c2) * W >= ubase * GT) ? 0 : 1;
+          rbase[k] = ((static_cast<long long>(c2) * 2 + which2) * 2 + ti) * BM + row;
+          ml[k] = (k < np) ? __ldcg(reinterpret_cast<const float2*>(p.ws_ml + rbase[k] * 2))
+                           : make_float2(-INFINITY, 0.f);
         }
+        float m_all = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < MAX_PIECES; ++k) m_all = fmaxf(m_all, ml[k].x);
+        float w[MAX_PIECES];
         float l_all = 0.f;
-        for (int c2 = c_lo; c2 <= c_hi; ++c2) {
-          float2 ml = make_float2(m_run, l_run);
-          if (c2 != cta) {
-            const int which2 = (range_begin(W, GT, c2) / p.n_tiles == rel) ? 0 : 1;
-            const long long slot2 = (static_cast<long long>(c2) * 2 + which2) * 2 + ti;
-            ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot2 * BM + row) * 2));
-          }
-          l_all = fmaf(ml.y, ex2_approx(ml.x - m_all), l_all);
+#pragma unroll
+        for (int k = 0; k < MAX_PIECES; ++k) {
+          w[k] = (k < np) ? ex2_approx(ml[k].x - m_all) : 0.f;
+          l_all = fmaf(ml[k].y, w[k], l_all);
         }
         const float inv = 1.f / l_all;
 #pragma unroll 1
         for (int c = 0; c < DP / 32; ++c) {
-          uint32_t own[32];
-          tmem_ld32(tO + 32 * c, own);
-          tmem_wait_ld();
-          reg_fence32(own);
           float acc[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) acc[e] = 0.f;
-          for (int c2 = c_lo; c2 <= c_hi; ++c2) {
-            if (c2 == cta) {
-              const float w = ex2_approx(m_run - m_all);
 #pragma unroll
-              for (int e = 0; e < 32; ++e) acc[e] = fmaf(__uint_as_float(own[e]), w, acc[e]);
-            } else {
-              const int which2 = (range_begin(W, GT, c2) / p.n_tiles == rel) ? 0 : 1;
-              const long long slot2 = (static_cast<long long>(c2) * 2 + which2) * 2 + ti;
-              const float w = ex2_approx(
-                  __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (slot2 * BM + row) * 2)).x - m_all);
-              const float4* src = reinterpret_cast<const float4*>(p.ws_o + (slot2 * BM + row) * DP + c * 32);
+          for (int k = 0; k < MAX_PIECES; ++k) {
+            if (k < np) {
+              const float4* src = reinterpret_cast<const float4*>(p.ws_o + rbase[k] * DP + c * 32);
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
                 const float4 v4 = __ldcg(src + e);
-                acc[4 * e] = fmaf(v4.x, w, acc[4 * e]);
-                acc[4 * e + 1] = fmaf(v4.y, w, acc[4 * e + 1]);
-                acc[4 * e + 2] = fmaf(v4.z, w, acc[4 * e + 2]);
-                acc[4 * e + 3] = fmaf(v4.w, w, acc[4 * e + 3]);
+                acc[4 * e] = fmaf(v4.x, w[k], acc[4 * e]);
+                acc[4 * e + 1] = fmaf(v4.y, w[k], acc[4 * e + 1]);
+                acc[4 * e + 2] = fmaf(v4.z, w[k], acc[4 * e + 2]);
+                acc[4 * e + 3] = fmaf(v4.w, w[k], acc[4 * e + 3]);
               }
             }
           }
@@ -1186,7 +1187,7 @@ struct Plan {
 };
 constexpr int kMinSplitSteps = 4;   // shortest key range a CTA gets in the tail
 constexpr int kMinSplitTiles = 16;      // fewer units than SMs: split units of >= 16 key tiles
-constexpr int kMinSplitTilesTail = 64;  // a partial last wave: split units of >= 64 key tiles
+constexpr int kMinSplitTilesTail = 128; // a partial last wave: split units of >= 128 key tiles
 
 bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Plan* pl) {
   pl->n_qb = (Sq + 2 * fa::BM - 1) / (2 * fa::BM);
@@ -1200,9 +1201,11 @@ bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Pla
   // Split the tail's key range over the CTAs when whole units would leave SMs
   // idle in the last wave and units are long enough to amortise writing and
   // combining partial results: >= 16 key tiles when there are fewer units than
-  // SMs, >= 64 otherwise. Measured on B200 (TFLOP/s, whole -> split):
-  // 1x16384x131072 D64 (64 units) 275 -> 614; 1x131072^2 D64 (512 units,
-  // 1024 key tiles) 544 -> 634; B1 H24 S4096 D128 (32 key tiles) 950 -> 908.
+  // SMs, >= 128 otherwise. Measured on B200 (TFLOP/s, whole -> split):
+  // 1x16384x131072 D64 (64 units) 292 -> 668; 1x131072^2 D64 (512 units,
+  // 1024 key tiles) 593 -> 688; 1x32768^2 D64 (128 units) 587 -> 649;
+  // B1 H8 S8192 D128 (64 key tiles) 1069 -> 1045; B1 H24 S4096 D128 (32 key
+  // tiles) 1028 -> 969.
   const bool long_units = pl->n_tiles >= (waves == 0 ? kMinSplitTiles : kMinSplitTilesTail);
   pl->split = (allow_split && tail > 0 && long_units) ? 1 : 0;
   if (pl->split) {
@@ -1210,6 +1213,9 @@ bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Pla
     pl->total_steps = tail * pl->n_tiles;
     long long gt = (pl->total_steps + kMinSplitSteps - 1) / kMinSplitSteps;
     if (gt > G) gt = G;
+    // every CTA range is at least tail*T/gt >= T/(MAX_PIECES-1) steps long, so a
+    // unit spans at most MAX_PIECES ranges
+    if (gt > (fa::MAX_PIECES - 1) * tail) gt = (fa::MAX_PIECES - 1) * tail;
     pl->tail_ctas = static_cast<int>(gt);
     pl->G = static_cast<int>(waves > 0 ? G : gt);
   } else {

@@ -71,12 +71,12 @@ def test_workspace_size_and_checks(lib):
     assert lib.workspace_size(2, 16, 4096, 1024, 128) == 0  # 8 key tiles per unit: never split
     assert lib.workspace_size(1, 24, 4096, 4096, 128) == 0  # 32 key tiles: the tail is not split
     assert lib.workspace_size(1, 1, 131072, 131072, 64) > 0  # 1024 key tiles: the tail is split
-    n = lib.workspace_size(1, 8, 8192, 8192, 128)  # 192 units on 148 SMs: split
+    n = lib.workspace_size(1, 8, 16384, 16384, 128)  # 512 units of 128 key tiles: tail split
     assert n > 0
-    q, k, v = make_qkv(1, 8, 8192, 8192, 128, device="cuda")
+    q, k, v = make_qkv(1, 8, 16384, 16384, 128, device="cuda")
     o = torch.empty_like(q)
     small = torch.zeros(256, dtype=torch.uint8, device="cuda")
-    rc = lib.launch_ws_status(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 1, 8, 8192, 8192, 128,
+    rc = lib.launch_ws_status(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 1, 8, 16384, 16384, 128,
                               0.1, small.data_ptr(), 256, torch.cuda.current_stream().cuda_stream)
     assert rc == STATUS["EINVAL"]
     assert lib.device_status(reset=False) == STATUS["OK"]
@@ -84,7 +84,7 @@ def test_workspace_size_and_checks(lib):
 
 def test_workspace_contents_do_not_matter(lib):
     """Garbage in the workspace (any bytes, earlier calls of other sizes) changes nothing."""
-    shape = (1, 8, 8192, 8192, 128)
+    shape = (1, 4, 16384, 16384, 128)
     B, H, Sq, Skv, D = shape
     q, k, v = make_qkv(B, H, Sq, Skv, D, seed=5)
     qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
