@@ -119,7 +119,8 @@ struct Cfg {
   static constexpr int B_KV_EMPTY = 4 + STAGES;
   static constexpr int B_S_FULL = 4 + 2 * STAGES;
   static constexpr int B_P_FULL = B_S_FULL + 2;
-  static constexpr int B_O_FULL = B_P_FULL + 2;
+  static constexpr int B_P_HALF = B_P_FULL + 2;  // [2]: first half of P stored
+  static constexpr int B_O_FULL = B_P_HALF + 2;
   static constexpr int B_WG = B_O_FULL + 2;  // per-warpgroup rendezvous, 2 barriers
   static constexpr int B_DRAIN = B_WG + 2;
   static constexpr int NUM_BARS = B_DRAIN + 1;
@@ -232,9 +233,13 @@ __device__ __forceinline__ float row_extreme(const uint32_t* s, int nvalid, bool
 // fp32 row sum in two partial sums. EMU_PAIRS of every 4 column pairs use the
 // FMA-pipe polynomial, the rest MUFU. MASK zeroes columns >= nvalid (last
 // key tile).
-template <bool MASK>
+// When half_bar is non-zero, the first half of P (keys 0..63) is published on
+// it as soon as it is stored (after before_half() has run), so the tensor core
+// can start on those keys while the second half is computed.
+template <bool MASK, typename BeforeHalf>
 __device__ __forceinline__ void row_exp_store(const uint32_t* s, float sl2, float neg_m, int nvalid,
-                                              uint32_t tS, float& sum0, float& sum1) {
+                                              uint32_t tS, float& sum0, float& sum1, uint32_t half_bar,
+                                              BeforeHalf&& before_half) {
   const uint64_t sl2x2 = f2_pack(sl2, sl2);
   const uint64_t negm2 = f2_pack(neg_m, neg_m);
   uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
@@ -264,6 +269,12 @@ __device__ __forceinline__ void row_exp_store(const uint32_t* s, float sl2, floa
       pk[c2] = pack_half2(e0, e1);
     }
     tmem_st32(tS + 32 * h, pk);
+    if (h == 0 && half_bar) {
+      before_half();
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(half_bar);
+    }
   }
   float a, b, c, d;
   f2_unpack(acc0, a, b);
@@ -370,6 +381,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(bars + 8 * (C::B_S_FULL + i), 1);
       mbar_init(bars + 8 * (C::B_P_FULL + i), BM);
+      mbar_init(bars + 8 * (C::B_P_HALF + i), BM);
       mbar_init(bars + 8 * (C::B_O_FULL + i), 1);
       mbar_init(bars + 8 * (C::B_WG + i), BM);
       last_flag[i] = 0;
@@ -491,11 +503,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mma_f16_ss_warp(d_tmem, dq + off, dK + ((kv_off >> 4) + off), IDESC_QK, k > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](uint32_t d_tmem, uint32_t p_tmem, uint32_t v_off, bool acc) {
+      // PV in two halves: keys 0-63 once the first half of P is stored
+      // (P_HALF), keys 64-127 once all of it is (P_FULL). Each barrier
+      // completes once per tile, so a parity never falls two phases behind.
+      auto issue_pv = [&](uint32_t d_tmem, uint32_t p_tmem, uint32_t v_off, bool acc, int ptile,
+                          uint32_t par) -> bool {
 #pragma unroll
-        for (int k = 0; k < BN / 16; ++k)
-          mma_f16_ts_warp(d_tmem, p_tmem + 8 * k, dV + ((v_off + k * 2048) >> 4), idesc_pv,
-                     (acc || k > 0) ? 1u : 0u);
+        for (int hh = 0; hh < 2; ++hh) {
+          if (!bwait_warp(bars, (hh ? C::B_P_FULL : C::B_P_HALF) + ptile, par, abort_flag, tmo, ROLE_MMA))
+            return false;
+          tc_fence_after();
+#pragma unroll
+          for (int k = 4 * hh; k < 4 * hh + 4; ++k)
+            mma_f16_ts_warp(d_tmem, p_tmem + 8 * k, dV + ((v_off + k * 2048) >> 4), idesc_pv,
+                            (acc || k > 0) ? 1u : 0u);
+        }
+        return true;
       };
 
       SegIter si;
@@ -529,9 +552,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_commit_warp(bars + 8 * (C::B_S_FULL + 0));
           if (has1) {
             if (j > t0) {
-              if (!bwait_warp(bars, C::B_P_FULL + 1, (g1 - 1) & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
-              tc_fence_after();
-              issue_pv(tO1, tS1, prev_v_slot * C::TILE_BYTES, j - 1 > t0);
+              if (!issue_pv(tO1, tS1, prev_v_slot * C::TILE_BYTES, j - 1 > t0, 1, (g1 - 1) & 1)) {
+                ok = false;
+                break;
+              }
               tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));  // V(j-1) free
             }
             issue_qk(tS1, dQ1, k_slot * C::TILE_BYTES);
@@ -541,18 +565,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + k_slot));  // K(j) free
           if (j + 1 == t1) tc_commit_warp(bars + 8 * (C::B_Q_EMPTY + qb));  // last S of this segment issued
           if (!bwait_warp(bars, C::B_KV_FULL + v_slot, v_ph, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
-          if (!bwait_warp(bars, C::B_P_FULL + 0, g0 & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(tO0, tS0, v_slot * C::TILE_BYTES, j > t0);
+          if (!issue_pv(tO0, tS0, v_slot * C::TILE_BYTES, j > t0, 0, g0 & 1)) { ok = false; break; }
           ++g0;
           if (j + 1 == t1) tc_commit_warp(bars + 8 * (C::B_O_FULL + 0));  // tile 0 epilogue may start
           if (!has1) tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + v_slot));
           prev_v_slot = v_slot;
         }
         if (ok && has1) {
-          if (bwait_warp(bars, C::B_P_FULL + 1, (g1 - 1) & 1, abort_flag, tmo, ROLE_MMA)) {
-            tc_fence_after();
-            issue_pv(tO1, tS1, prev_v_slot * C::TILE_BYTES, t1 - 1 > t0);
+          if (issue_pv(tO1, tS1, prev_v_slot * C::TILE_BYTES, t1 - 1 > t0, 1, (g1 - 1) & 1)) {
             tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + prev_v_slot));
           } else {
             ok = false;
@@ -619,17 +639,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           factor = ex2_approx(m_run - m_new);  // 0 on the first tile (m_run = -inf)
           m_run = m_new;
         }
-        l_run *= factor;
-        const float neg_m = -m_run;
-        float lsum0, lsum1;
-        if (full)
-          row_exp_store<false>(s, sl2, neg_m, nvalid, tS, lsum0, lsum1);
-        else
-          row_exp_store<true>(s, sl2, neg_m, nvalid, tS, lsum0, lsum1);
-        l_run += lsum0 + lsum1;
-        // Rescale this warp's O rows when any of them moved its max. PV(j-1)
-        // of this tile completed before S(j) was signalled, and PV(j) is only
-        // issued after this warpgroup arrives on P_FULL below.
+        // Rescale this warp's O rows when any of them moved its max, before any
+        // of P is published. PV(j-1) of this tile completed before S(j) was
+        // signalled; PV(j) waits for the P barriers.
         if (j > t0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll
           for (int c = 0; c < DP / 32; ++c) {
@@ -642,6 +654,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_st32(tO + 32 * c, o);
           }
         }
+        l_run *= factor;
+        const float neg_m = -m_run;
+        const uint32_t half_bar = bars + 8 * (C::B_P_HALF + ti);
+        float lsum0, lsum1;
+        if (full)
+          row_exp_store<false>(s, sl2, neg_m, nvalid, tS, lsum0, lsum1, half_bar, [] {});
+        else
+          row_exp_store<true>(s, sl2, neg_m, nvalid, tS, lsum0, lsum1, half_bar, [] {});
+        l_run += lsum0 + lsum1;
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(bars + 8 * (C::B_P_FULL + ti));
@@ -999,9 +1020,9 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
       l_run *= factor;
       float lsum0, lsum1;
       if (full)
-        row_exp_store<false>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1);
+        row_exp_store<false>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {});
       else
-        row_exp_store<true>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1);
+        row_exp_store<true>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {});
       l_run += lsum0 + lsum1;
       // O may only be rescaled once PV(j-1) has completed.
       if (j > 0) {
