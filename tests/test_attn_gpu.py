@@ -206,3 +206,18 @@ def test_d512_non_contiguous_vae_layout(op):
     q4, k4, v4 = qf.unsqueeze(1), kf.unsqueeze(1), vf.unsqueeze(1)
     out = op.attn(q4.cuda(), k4.cuda(), v4.cuda(), D ** -0.5).cpu()
     check_rows(out, q4.contiguous(), k4.contiguous(), v4.contiguous(), D ** -0.5, what="d512 noncontig")
+
+
+def test_d512_very_long_sequence(op):
+    """bench_d512.py:63-79: S=129600 at D=512 (one head) in O(S*D) memory."""
+    S = 129600
+    q, k, v = make_qkv(1, 1, S, S, 512, seed=15, device="cuda")
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    out = op.attn(q, k, v, 512 ** -0.5)
+    torch.cuda.synchronize()
+    peak = torch.cuda.max_memory_allocated() - base
+    assert peak <= out.numel() * 2 + (1 << 20), peak  # the D=512 kernel uses no workspace
+    rows = sample_rows(S, n_each=24, seed=15)
+    check_rows(out.cpu(), q.cpu(), k.cpu(), v.cpu(), 512 ** -0.5, rows, what="S=129600 D512")
