@@ -44,8 +44,10 @@
 #include <math.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <unistd.h>
 
 #include <atomic>
+#include <chrono>
 #include <mutex>
 
 #include "../../include/gfx906_b200_attn.h"
@@ -1194,7 +1196,22 @@ unsigned long long timeout_ns_from_env() {
 }
 
 // Launch epochs tag the split counters (56 bits: never reused in practice).
-std::atomic<unsigned long long> g_epoch{1};
+// The sequence starts at a per-process, per-load pseudo-random point (clock,
+// pid and this library's load address through the splitmix64 finaliser), so
+// that two instances of the library -- two copies loaded in one process, or
+// a workspace handed on from another user -- do not issue the same epochs
+// and mistake each other's counters for their own.
+unsigned long long seed_epoch() {
+  uint64_t x = static_cast<uint64_t>(std::chrono::steady_clock::now().time_since_epoch().count());
+  x ^= static_cast<uint64_t>(getpid()) << 40;
+  x ^= static_cast<uint64_t>(reinterpret_cast<uintptr_t>(&seed_epoch));
+  x += 0x9e3779b97f4a7c15ull;
+  x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ull;
+  x = (x ^ (x >> 27)) * 0x94d049bb133111ebull;
+  x ^= x >> 31;
+  return x & ((1ull << 56) - 1);
+}
+std::atomic<unsigned long long> g_epoch{seed_epoch()};
 unsigned long long next_epoch() { return g_epoch.fetch_add(1) & ((1ull << 56) - 1); }
 
 // Persistent schedule of attn_fwd_kernel (see SegIter in the kernel).

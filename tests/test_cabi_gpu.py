@@ -114,3 +114,36 @@ def test_workspace_contents_do_not_matter(lib):
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
     check_rows(outs[0], q, k, v, D ** -0.5, sample_rows(Sq, n_each=64, seed=3), what="ws garbage")
+
+
+def test_workspace_shared_between_library_instances(lib, tmp_path):
+    """A second copy of the library (its own launch epochs) reuses a workspace
+    the first one left behind: its split counters must not be mistaken for
+    the new launch's."""
+    import shutil
+
+    copy = tmp_path / "libgfx906_b200_attn_copy.so"
+    shutil.copy(build.LIB_PATH, copy)
+    lib2 = CABI(str(copy))
+    shape = (1, 4, 16384, 16384, 128)
+    B, H, Sq, Skv, D = shape
+    q, k, v = make_qkv(B, H, Sq, Skv, D, seed=8)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    n = lib.workspace_size(B, H, Sq, Skv, D)
+    assert n > 0 and lib2.workspace_size(B, H, Sq, Skv, D) == n
+    ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for which in (lib, lib2, lib, lib2):
+        o = torch.full_like(qd, float("nan"))
+        rc = which.launch_ws_status(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), o.data_ptr(), B, H, Sq, Skv, D,
+                                    D ** -0.5, ws.data_ptr(), n, st)
+        assert rc == STATUS["OK"]
+        torch.cuda.synchronize()
+        outs.append(o.cpu())
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    assert not torch.isnan(outs[0]).any()
+    check_rows(outs[0], q, k, v, D ** -0.5, sample_rows(Sq, n_each=32, seed=8), what="two library instances")
+    assert lib.device_status(reset=False) == STATUS["OK"]
+    assert lib2.device_status(reset=False) == STATUS["OK"]
