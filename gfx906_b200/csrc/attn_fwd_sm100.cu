@@ -643,17 +643,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         // Rescale this warp's O rows when any of them moved its max, before any
         // of P is published. PV(j-1) of this tile completed before S(j) was
-        // signalled; PV(j) waits for the P barriers.
+        // signalled; PV(j) waits for the P barriers. 16 columns at a time: the
+        // whole score row is live here, and 32 more registers would spill
+        // (measured on B200: the spill-free form is 4-7% faster at D=128).
         if (j > t0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll
-          for (int c = 0; c < DP / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + 32 * c, o);
+          for (int c = 0; c < DP / 16; ++c) {
+            uint32_t o[16];
+            tmem_ld16(tO + 16 * c, o);
             tmem_wait_ld();
-            reg_fence32(o);
+            reg_fence16(o);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
-            tmem_st32(tO + 32 * c, o);
+            for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+            tmem_st16(tO + 16 * c, o);
           }
         }
         l_run *= factor;
