@@ -16,9 +16,11 @@ sets that their total is larger than the 126 MB L2, so no step reads inputs
 the previous step left in L2. SM clocks and throttle reasons are sampled
 through NVML while the timed steps run.
 
-`e2e` repeats the measurement through the public operator with the inputs in
-pinned host memory: each step copies q, k, v host->device, runs the operator
-and copies o back, all inside the timed region.
+`e2e` repeats the measurement through the public host-memory entry point
+(`gfx906_b200.attn_host`) with the inputs in pinned host memory: each step
+copies all of q, k, v host->device and all of o back, inside the timed
+region; the copies of one block of (batch x head) units overlap the kernel of
+the previous block and the download of the one before.
 
 `--impl reference` times the reference's CPU path (fp32 SDPA MATH on the host
 cores, from the CPU oracle) on a bounded sample of the same workload.
@@ -370,11 +372,9 @@ def run_ours(args, rank, world, local):
     e2e_steps = max(1, args.e2e_steps)
 
     def e2e_step():
-        dq = hq.to(dev, non_blocking=True)
-        dk = hk.to(dev, non_blocking=True)
-        dv = hv.to(dev, non_blocking=True)
-        o = gfx906_b200.attn(dq, dk, dv, scale)
-        hout.copy_(o, non_blocking=True)
+        # public host-memory entry point: every step uploads q, k, v and downloads
+        # o; blocks of (batch x head) units overlap upload, kernel and download
+        gfx906_b200.attn_host(hq, hk, hv, scale, out=hout, non_blocking=True)
 
     for _ in range(3):
         e2e_step()

@@ -8,11 +8,14 @@ Public entry points:
   reference's ``deploy/gfx906_attn.py`` (returns None instead of raising).
 * ``gfx906_attention.install()``: the ComfyUI hook with eligibility gating and
   stock fallback, as in the reference's ``deploy/gfx906_attention.py``.
+* ``attn_host(q, k, v, scale)``: the same operator for q, k, v in (pinned)
+  host memory, uploads and downloads overlapped with the kernel per block of
+  (batch x head) units (``host.py``).
 """
 
 from .gfx906_attn import is_sm100, last_error, load_attention
 
-__all__ = ["attn", "device_status", "is_sm100", "load_attention", "last_error"]
+__all__ = ["attn", "attn_host", "device_status", "is_sm100", "load_attention", "last_error"]
 
 
 def _module_or_raise():
@@ -30,3 +33,10 @@ def attn(q, k, v, scale):
 def device_status(reset: bool = False) -> int:
     """0 unless a kernel wait timed out since the last reset (synchronises)."""
     return _module_or_raise().device_status(reset)
+
+
+def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=False):
+    """The operator on host tensors with the PCIe copies overlapped (see ``host.attn_host``)."""
+    from .host import attn_host as _attn_host
+
+    return _attn_host(q, k, v, scale, out=out, device=device, blocks=blocks, non_blocking=non_blocking)

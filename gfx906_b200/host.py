@@ -1,0 +1,111 @@
+"""Attention on tensors that live in host memory, with the PCIe copies overlapped.
+
+The operator itself (``gfx906_b200.attn``) takes CUDA tensors, like the
+reference's ``attn.cpp``. A caller whose q, k, v are in host memory otherwise
+pays upload, compute and download one after the other. ``attn_host`` cuts the
+(batch x head) units into contiguous blocks and runs, on three CUDA streams,
+the upload of block i+1, the attention of block i and the download of block
+i-1 at the same time (PCIe moves data in both directions at once). Every byte
+of q, k, v and o still crosses the bus on every call.
+
+Blocks are contiguous in the flattened b * H + h index, so each block's q, k,
+v and o are single contiguous ranges of the [B, H, S, D] tensors.
+"""
+
+from __future__ import annotations
+
+import threading
+
+import torch
+
+__all__ = ["attn_host"]
+
+_streams = {}
+_streams_lock = threading.Lock()
+
+
+def _side_streams(device: torch.device):
+    """One upload and one download stream per device, created on first use."""
+    key = device.index
+    with _streams_lock:
+        pair = _streams.get(key)
+        if pair is None:
+            pair = (torch.cuda.Stream(device=device), torch.cuda.Stream(device=device))
+            _streams[key] = pair
+    return pair
+
+
+def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=False):
+    """O = softmax(scale * q @ k^T) @ v for fp16 [B,H,S,D] tensors in host memory.
+
+    q: [B, H, Sq, D]; k, v: [B, H, Skv, D]; all fp16 CPU tensors, contiguous.
+    Pinned memory (``tensor.pin_memory()``) is what lets the copies overlap the
+    kernel; pageable tensors work but their copies serialise.
+    out: optional [B, H, Sq, D] fp16 CPU tensor for the result (allocated
+    pinned when None). device: the CUDA device (default: the current one).
+    blocks: number of (batch x head) blocks (default min(B*H, 8)).
+    non_blocking: when False the call returns with ``out`` filled; when True it
+    returns at once and the current CUDA stream is made to wait for the last
+    download, so ``out`` is valid once that stream has been synchronised.
+    """
+    from . import attn  # the strict operator: raises if the native code is missing
+
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.is_cuda:
+            raise ValueError(f"attn_host: {name} must be a host tensor (use gfx906_b200.attn for CUDA tensors)")
+        if t.dim() != 4 or t.dtype != torch.float16 or not t.is_contiguous():
+            raise ValueError(f"attn_host: {name} must be a contiguous fp16 [B,H,S,D] tensor")
+    B, H, Sq, D = q.shape
+    if k.shape[:2] != (B, H) or v.shape != k.shape or k.shape[3] != D:
+        raise ValueError("attn_host: k and v must be [B, H, Skv, D] matching q")
+    if not torch.cuda.is_available():
+        raise RuntimeError("attn_host: CUDA is not available")
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    elif out.shape != q.shape or out.dtype != q.dtype or out.is_cuda or not out.is_contiguous():
+        raise ValueError("attn_host: out must be a contiguous fp16 host tensor shaped like q")
+    units = B * H
+    if units == 0 or Sq == 0:
+        return out
+    Skv = k.shape[2]
+    nb = max(1, min(units, 8 if blocks is None else int(blocks)))
+    qf, kf, vf, of = (t.view(units, -1, D) for t in (q, k, v, out))
+
+    with torch.cuda.device(dev):
+        compute = torch.cuda.current_stream(dev)
+        up, down = _side_streams(dev)
+        # The device buffers are allocated on the compute stream; the side
+        # streams are recorded on them so that the caching allocator does not
+        # hand them out again before the copies queued there have finished.
+        dq = torch.empty((units, Sq, D), dtype=q.dtype, device=dev)
+        dk = torch.empty((units, Skv, D), dtype=q.dtype, device=dev)
+        dv = torch.empty((units, Skv, D), dtype=q.dtype, device=dev)
+        up.wait_stream(compute)  # the buffers' previous users, if any, are done
+        done = None
+        for i in range(nb):
+            lo, hi = units * i // nb, units * (i + 1) // nb
+            if hi == lo:
+                continue
+            with torch.cuda.stream(up):
+                dq[lo:hi].copy_(qf[lo:hi], non_blocking=True)
+                dk[lo:hi].copy_(kf[lo:hi], non_blocking=True)
+                dv[lo:hi].copy_(vf[lo:hi], non_blocking=True)
+                uploaded = torch.cuda.Event()
+                uploaded.record(up)
+            compute.wait_event(uploaded)
+            o = attn(dq[lo:hi].unsqueeze(0), dk[lo:hi].unsqueeze(0), dv[lo:hi].unsqueeze(0), scale)
+            computed = torch.cuda.Event()
+            computed.record(compute)
+            with torch.cuda.stream(down):
+                down.wait_event(computed)
+                of[lo:hi].copy_(o.squeeze(0), non_blocking=True)
+                o.record_stream(down)
+                done = torch.cuda.Event()
+                done.record(down)
+        for t in (dq, dk, dv):
+            t.record_stream(up)
+        compute.wait_event(done)
+        if not non_blocking:
+            done.synchronize()
+    return out
