@@ -15,7 +15,7 @@ Public entry points:
 
 from .gfx906_attn import is_sm100, last_error, load_attention
 
-__all__ = ["attn", "attn_host", "device_status", "is_sm100", "load_attention", "last_error"]
+__all__ = ["attn", "attn_dmajor", "attn_host", "device_status", "is_sm100", "load_attention", "last_error"]
 
 
 def _module_or_raise():
@@ -28,6 +28,13 @@ def _module_or_raise():
 def attn(q, k, v, scale):
     """O = softmax(scale * q @ k^T) @ v on the sm_100a kernel (fp16 [B,H,S,D])."""
     return _module_or_raise().attn(q, k, v, scale)
+
+
+def attn_dmajor(q, k, v, scale):
+    """The operator on transposed fp16 tensors: q [B,H,D,Sq], k, v [B,H,D,Skv],
+    D = 512, sequence innermost (a [b, c, h, w] feature map is [b, 1, c, h*w]);
+    returns o as [B,H,D,Sq]. Sq and Skv must be multiples of 8."""
+    return _module_or_raise().attn_dmajor(q, k, v, scale)
 
 
 def device_status(reset: bool = False) -> int:

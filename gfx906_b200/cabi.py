@@ -39,6 +39,8 @@ class CABI:
         d.gfx906_b200_attn_workspace_size.restype = ctypes.c_size_t
         d.gfx906_b200_attn_launch_ws.argtypes = sig[:-1] + [_c_void_p, ctypes.c_size_t, _c_void_p]
         d.gfx906_b200_attn_launch_ws.restype = _c_int
+        d.gfx906_b200_attn_launch_dmajor.argtypes = sig
+        d.gfx906_b200_attn_launch_dmajor.restype = _c_int
         d.gfx906_b200_attn_launch_noalloc.argtypes = sig
         d.gfx906_b200_attn_launch_noalloc.restype = _c_int
         d.gfx906_b200_attn_noalloc_capacity.argtypes = []
@@ -55,6 +57,9 @@ class CABI:
 
     def launch_noalloc_status(self, q, k, v, o, B, H, Sq, Skv, D, scale, stream=None) -> int:
         return self.dll.gfx906_b200_attn_launch_noalloc(q, k, v, o, B, H, Sq, Skv, D, _c_float(scale), stream)
+
+    def launch_dmajor_status(self, q, k, v, o, B, H, Sq, Skv, D, scale, stream=None) -> int:
+        return self.dll.gfx906_b200_attn_launch_dmajor(q, k, v, o, B, H, Sq, Skv, D, _c_float(scale), stream)
 
     def workspace_size(self, B, H, Sq, Skv, D) -> int:
         return self.dll.gfx906_b200_attn_workspace_size(B, H, Sq, Skv, D)

@@ -66,11 +66,44 @@ torch::Tensor attn(torch::Tensor q, torch::Tensor k, torch::Tensor v, double sca
   return o;
 }
 
+// Attention on transposed ("d-major") tensors: q [B,H,D,Sq], k and v
+// [B,H,D,Skv], D = 512, sequence innermost; returns o as [B,H,D,Sq]. A
+// [b, c, h, w] feature map viewed as [b, 1, c, h*w] is this layout, so the VAE
+// mid-block attention runs without transposing anything. Inputs are made
+// contiguous in this layout (a no-op for feature maps). Sq and Skv must be
+// multiples of 8.
+torch::Tensor attn_dmajor(torch::Tensor q, torch::Tensor k, torch::Tensor v, double scale) {
+  TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda() && q.dtype() == torch::kHalf &&
+                  k.dtype() == torch::kHalf && v.dtype() == torch::kHalf,
+              "kernel: q, k and v must be CUDA float16 tensors");
+  TORCH_CHECK(k.device() == q.device() && v.device() == q.device(),
+              "kernel: q, k and v must be on the same device");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "kernel: q/k/v must be [B,H,D,S]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(k.sizes() == v.sizes() && q.size(0) == k.size(0) && q.size(1) == k.size(1) &&
+                  q.size(2) == k.size(2),
+              "kernel: q/k/v shape mismatch");
+  const auto B = q.size(0), H = q.size(1), D = q.size(2), Sq = q.size(3), Skv = k.size(3);
+  TORCH_CHECK(D == 512, "kernel: the transposed layout needs head_dim 512");
+  TORCH_CHECK(Sq % 8 == 0 && Skv % 8 == 0, "kernel: the transposed layout needs sequence lengths % 8 == 0");
+  TORCH_CHECK(B <= INT32_MAX && H <= INT32_MAX && Sq <= INT32_MAX && Skv <= INT32_MAX,
+              "kernel: sizes must fit in int32");
+  auto qc = q.contiguous(), kc = k.contiguous(), vc = v.contiguous();
+  auto o = torch::empty_like(qc);
+  const int rc = gfx906_b200_attn_launch_dmajor(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), o.data_ptr(),
+                                                static_cast<int>(B), static_cast<int>(H), static_cast<int>(Sq),
+                                                static_cast<int>(Skv), static_cast<int>(D),
+                                                static_cast<float>(scale), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == GFX906_B200_OK, "kernel: ", gfx906_b200_attn_error_string(rc));
+  return o;
+}
+
 // Device status word of the current device (see gfx906_b200_attn_device_status).
 // Returns 0 when no kernel wait has timed out. Synchronises.
 int64_t device_status(bool reset) { return gfx906_b200_attn_device_status(reset ? 1 : 0); }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn", &attn, "flash-attention forward (fp16 [B,H,S,D], sm_100a)");
+  m.def("attn_dmajor", &attn_dmajor, "flash-attention forward on transposed [B,H,D,S] fp16, D = 512");
   m.def("device_status", &device_status, "device status word (0 = ok)", pybind11::arg("reset") = false);
 }

@@ -815,6 +815,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // O half at [256,512); P of tile j is written over the first 64 columns of
 // its S buffer. MMA order: S(0), S(1), PV(0), S(2), PV(1), ... so the tensor
 // core computes S(j+1) while the softmax warpgroup works on S(j).
+//
+// DMAJOR: every (b, h) matrix is stored transposed, [D][S] with the sequence
+// contiguous -- a [b, c, h, w] feature map is exactly this with H = 1, D = c,
+// S = h * w -- and the kernel reads and writes that layout directly: Q and K
+// become MN-major MMA operands (64 sequence positions per 128-byte row, head
+// dims down the rows), V a K-major one, and O is staged as [256 d][128 rows]
+// and written with one unswizzled TMA store. Nothing is transposed in memory.
 struct Cfg512 {
   static constexpr int SLOTS = 3;
   static constexpr int SLOT_BYTES = 2 * CHUNK_BYTES;
@@ -828,6 +835,7 @@ struct Cfg512 {
   static constexpr int THREADS = 256;  // softmax warpgroup + control warpgroup
 };
 
+template <bool DMAJOR>
 __global__ void __launch_bounds__(Cfg512::THREADS, 1)
     attn_fwd_d512_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -889,7 +897,14 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_o);
       mbar_arrive_expect_tx_warp(bars + 8 * C::B_Q, C::Q_BYTES);
-      for (int c = 0; c < 8; ++c) tma_load_3d_warp(sQ + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q, c * 64, q_row0, bh);
+      if (DMAJOR) {
+        // [64 rows x 256 d] boxes: M-block mb (rows 64 mb ..) at 64 KiB * mb, d rows of 128 B
+        for (int mb = 0; mb < 2; ++mb)
+          for (int dd = 0; dd < 2; ++dd)
+            tma_load_3d_warp(sQ + mb * 65536 + dd * 32768, &tm_q, bars + 8 * C::B_Q, q_row0 + 64 * mb, 256 * dd, bh);
+      } else {
+        for (int c = 0; c < 8; ++c) tma_load_3d_warp(sQ + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q, c * 64, q_row0, bh);
+      }
       int it = 0;
       bool ok = true;
       // slot order: K(0); then K(j), V(j-1) for j >= 1; then V(n-1)
@@ -899,8 +914,13 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
         if (!bwait_warp(bars, C::B_KV_EMPTY + slot, ph ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) return false;
         const uint32_t full = bars + 8 * (C::B_KV_FULL + slot);
         mbar_arrive_expect_tx_warp(full, C::SLOT_BYTES);
-        tma_load_3d_warp(sRing + slot * C::SLOT_BYTES, m, full, d0, key0, bh);
-        tma_load_3d_warp(sRing + slot * C::SLOT_BYTES + CHUNK_BYTES, m, full, d0 + 64, key0, bh);
+        if (DMAJOR) {  // [64 keys x 128 d] boxes, keys 0-63 then 64-127
+          tma_load_3d_warp(sRing + slot * C::SLOT_BYTES, m, full, key0, d0, bh);
+          tma_load_3d_warp(sRing + slot * C::SLOT_BYTES + CHUNK_BYTES, m, full, key0 + 64, d0, bh);
+        } else {       // [128 keys x 64 d] boxes, d0 .. d0+63 then d0+64 ..
+          tma_load_3d_warp(sRing + slot * C::SLOT_BYTES, m, full, d0, key0, bh);
+          tma_load_3d_warp(sRing + slot * C::SLOT_BYTES + CHUNK_BYTES, m, full, d0 + 64, key0, bh);
+        }
         ++it;
         return true;
       };
@@ -928,11 +948,13 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
     // ----------------------------------------------------------- MMA issuer
     // Whole-warp issue loop, one elected lane per tcgen05 instruction.
     {
-      constexpr uint32_t IDESC_QK = idesc_f16_f32(BM, BN, 0, 0);
-      constexpr uint32_t IDESC_PV = idesc_f16_f32(BM, 128, 0, 1);
-      const uint64_t dQ = sdesc_sw128(sQ, 16, 1024);
-      const uint64_t dK = sdesc_sw128(sRing, 16, 1024);
-      const uint64_t dV = sdesc_sw128(sRing, CHUNK_BYTES, 1024);
+      // Row-major: Q and K K-major, V MN-major. DMAJOR: Q and K MN-major (the
+      // leading byte offset steps to the second 64-wide M / N block), V K-major.
+      constexpr uint32_t IDESC_QK = idesc_f16_f32(BM, BN, DMAJOR ? 1 : 0, DMAJOR ? 1 : 0);
+      constexpr uint32_t IDESC_PV = idesc_f16_f32(BM, 128, 0, DMAJOR ? 0 : 1);
+      const uint64_t dQ = sdesc_sw128(sQ, DMAJOR ? 65536 : 16, 1024);
+      const uint64_t dK = sdesc_sw128(sRing, DMAJOR ? CHUNK_BYTES : 16, 1024);
+      const uint64_t dV = sdesc_sw128(sRing, DMAJOR ? 16 : CHUNK_BYTES, 1024);
       const uint32_t tO = tmem + 256;
       int it = 0;
       bool ok = bwait_warp(bars, C::B_Q, 0, abort_flag, tmo, ROLE_MMA);
@@ -953,8 +975,11 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
           const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
-            const uint32_t qoff = static_cast<uint32_t>((2 * s + (k >> 2)) * CHUNK_BYTES + (k & 3) * 32) >> 4;
-            const uint32_t koff = soff + (static_cast<uint32_t>((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4);
+            // DMAJOR: 16 head dims = 16 rows of 128 B; row-major: 32-byte steps in a 64-d box
+            const uint32_t qoff = DMAJOR ? static_cast<uint32_t>((8 * s + k) * 2048) >> 4
+                                         : static_cast<uint32_t>((2 * s + (k >> 2)) * CHUNK_BYTES + (k & 3) * 32) >> 4;
+            const uint32_t koff = soff + (DMAJOR ? static_cast<uint32_t>(k * 2048) >> 4
+                                                 : static_cast<uint32_t>((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4);
             mma_f16_ss_warp(tS, dQ + qoff, dK + koff, IDESC_QK, (s > 0 || k > 0) ? 1u : 0u);
           }
           tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + slot));
@@ -971,9 +996,11 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
           if (!next_slot(slot)) return false;
           const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
 #pragma unroll
-          for (int k = 0; k < BN / 16; ++k)
-            mma_f16_ts_warp(tO + 128 * s, tP + 8 * k, dV + soff + ((k * 2048) >> 4), IDESC_PV,
-                       (j > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < BN / 16; ++k) {
+            const uint32_t voff = DMAJOR ? static_cast<uint32_t>((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4
+                                         : static_cast<uint32_t>(k * 2048) >> 4;
+            mma_f16_ts_warp(tO + 128 * s, tP + 8 * k, dV + soff + voff, IDESC_PV, (j > 0 || k > 0) ? 1u : 0u);
+          }
           tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + slot));
         }
         tc_commit_warp(bars + 8 * C::B_PV_DONE);
@@ -1061,21 +1088,31 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
         tmem_wait_ld();
         reg_fence32(o);
         reg_fence32(o + 32);
-        const uint32_t rowbase = sQ + c * CHUNK_BYTES + row * 128;  // Q is dead: its last MMA completed
+        // Q is dead (its last MMA completed): it becomes the staging buffer
+        if (DMAJOR) {  // [256 d][128 rows] fp16, row `row` is column `row`
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint32_t a = pack_half2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
-          const uint32_t bb = pack_half2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
-          const uint32_t cc = pack_half2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
-          const uint32_t d = pack_half2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
-          st_shared_v4(rowbase + ((u ^ (row & 7)) << 4), a, bb, cc, d);
+          for (int e = 0; e < 64; ++e)
+            st_shared_u16(sQ + ((64 * c + e) * BM + row) * 2, __half_as_ushort(__float2half_rn(__uint_as_float(o[e]) * inv)));
+        } else {
+          const uint32_t rowbase = sQ + c * CHUNK_BYTES + row * 128;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint32_t a = pack_half2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
+            const uint32_t bb = pack_half2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
+            const uint32_t cc = pack_half2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
+            const uint32_t d = pack_half2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
+            st_shared_v4(rowbase + ((u ^ (row & 7)) << 4), a, bb, cc, d);
+          }
         }
       }
       fence_proxy_async_smem();
     }
     mbar_arrive(bars + 8 * C::B_EPI);
     if (warp == 0 && lane == 0 && have_o && bwait(bars, C::B_EPI, 0, abort_flag, tmo, ROLE_SOFTMAX0)) {
-      for (int c = 0; c < 4; ++c) tma_store_3d(&tm_o, sQ + c * CHUNK_BYTES, 256 * half + 64 * c, q_row0, bh);
+      if (DMAJOR)
+        tma_store_3d(&tm_o, sQ, q_row0, 256 * half, bh);  // one [128 rows x 256 d] box
+      else
+        for (int c = 0; c < 4; ++c) tma_store_3d(&tm_o, sQ + c * CHUNK_BYTES, 256 * half + 64 * c, q_row0, bh);
       tma_store_commit();
       tma_store_wait_read0();
     }
@@ -1144,6 +1181,26 @@ bool make_map(CUtensorMap* m, const void* base, int D, int S, long long BH, int 
   return r == CUDA_SUCCESS;
 }
 
+// Transposed ("d-major") [B*H, D, S] fp16 tensor: the sequence is the
+// innermost, contiguous dimension. Boxes of box_s positions x box_d head dims.
+// 128B swizzle for MMA operand tiles (box_s = 64), none for the output store.
+bool make_map_dmajor(CUtensorMap* m, const void* base, int D, int S, long long BH, int box_s, int box_d,
+                     bool swizzle) {
+  auto enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t gdim[3] = {static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(D),
+                        static_cast<cuuint64_t>(BH)};
+  cuuint64_t gstride[2] = {static_cast<cuuint64_t>(S) * 2,
+                           static_cast<cuuint64_t>(S) * static_cast<cuuint64_t>(D) * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_s), static_cast<cuuint32_t>(box_d), 1};
+  cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), gdim, gstride, box,
+                   estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 struct DeviceInfo {
   bool checked = false;
   bool sm100 = false;
@@ -1176,7 +1233,9 @@ int check_device(int* dev_out) {
                              fa::Cfg<64>::SMEM_BYTES) != cudaSuccess ||
         cudaFuncSetAttribute(fa::attn_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              fa::Cfg<128>::SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(fa::attn_fwd_d512_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(fa::attn_fwd_d512_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             fa::Cfg512::SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(fa::attn_fwd_d512_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              fa::Cfg512::SMEM_BYTES) != cudaSuccess)
       return GFX906_B200_ECUDA;
     di.attrs_set = true;
@@ -1318,12 +1377,18 @@ int launch_dp(const void* q, const void* k, const void* v, void* o, long long BH
   return cudaGetLastError() == cudaSuccess ? GFX906_B200_OK : GFX906_B200_ECUDA;
 }
 
+template <bool DMAJOR>
 int launch_d512(const void* q, const void* k, const void* v, void* o, long long BH, int Sq, int Skv,
                 float scale, cudaStream_t stream) {
   CUtensorMap mq, mk, mv, mo;
-  if (!make_map(&mq, q, 512, Sq, BH, fa::BM) || !make_map(&mk, k, 512, Skv, BH, fa::BN) ||
-      !make_map(&mv, v, 512, Skv, BH, fa::BN) || !make_map(&mo, o, 512, Sq, BH, fa::BM))
+  if (DMAJOR) {
+    if (!make_map_dmajor(&mq, q, 512, Sq, BH, 64, 256, true) || !make_map_dmajor(&mk, k, 512, Skv, BH, 64, 128, true) ||
+        !make_map_dmajor(&mv, v, 512, Skv, BH, 64, 128, true) || !make_map_dmajor(&mo, o, 512, Sq, BH, fa::BM, 256, false))
+      return GFX906_B200_ECUDA;
+  } else if (!make_map(&mq, q, 512, Sq, BH, fa::BM) || !make_map(&mk, k, 512, Skv, BH, fa::BN) ||
+             !make_map(&mv, v, 512, Skv, BH, fa::BN) || !make_map(&mo, o, 512, Sq, BH, fa::BM)) {
     return GFX906_B200_ECUDA;
+  }
   fa::Params prm{};
   prm.Sq = Sq;
   prm.Skv = Skv;
@@ -1335,7 +1400,7 @@ int launch_d512(const void* q, const void* k, const void* v, void* o, long long 
     const long long n = (BH - off) < 65535 ? (BH - off) : 65535;
     prm.bh_offset = static_cast<int>(off);
     dim3 grid(2 * qtiles, static_cast<unsigned>(n), 1);
-    fa::attn_fwd_d512_kernel<<<grid, fa::Cfg512::THREADS, fa::Cfg512::SMEM_BYTES, stream>>>(mq, mk, mv, mo, prm);
+    fa::attn_fwd_d512_kernel<DMAJOR><<<grid, fa::Cfg512::THREADS, fa::Cfg512::SMEM_BYTES, stream>>>(mq, mk, mv, mo, prm);
     if (cudaGetLastError() != cudaSuccess) return GFX906_B200_ECUDA;
   }
   return GFX906_B200_OK;
@@ -1381,7 +1446,7 @@ int attn_launch_impl(const void* q, const void* k, const void* v, void* o, int B
   }
   if (D == 128) return launch_dp<128>(q, k, v, o, BH, Sq, Skv, D, scale, ws, ws_size, dev, stream);
   if (D <= 64) return launch_dp<64>(q, k, v, o, BH, Sq, Skv, D, scale, ws, ws_size, dev, stream);
-  return launch_d512(q, k, v, o, BH, Sq, Skv, scale, stream);
+  return launch_d512<false>(q, k, v, o, BH, Sq, Skv, scale, stream);
 }
 
 }  // namespace
@@ -1391,6 +1456,34 @@ extern "C" {
 int gfx906_b200_attn_launch(const void* q, const void* k, const void* v, void* o, int B, int H, int Sq,
                             int Skv, int D, float scale, cudaStream_t stream) {
   const int rc = attn_launch_impl(q, k, v, o, B, H, Sq, Skv, D, scale, nullptr, 0, stream);
+  t_last_error = rc;
+  return rc;
+}
+
+int gfx906_b200_attn_launch_dmajor(const void* q, const void* k, const void* v, void* o, int B, int H, int Sq,
+                                   int Skv, int D, float scale, cudaStream_t stream) {
+  bool skip = false;
+  int rc = check_args(q, k, v, o, B, H, Sq, Skv, D, &skip);
+  if (rc == GFX906_B200_OK && !skip) {
+    if (D != 512) {
+      rc = GFX906_B200_EHEADDIM;
+    } else if (Sq % 8 != 0 || Skv % 8 != 0) {
+      rc = GFX906_B200_EALIGN;  // every [D][S] row must start on 16 bytes for TMA
+    } else {
+      int dev = 0;
+      rc = check_device(&dev);
+      if (rc == GFX906_B200_OK) {
+        const long long BH = static_cast<long long>(B) * H;
+        if (Skv == 0) {
+          rc = cudaMemsetAsync(o, 0, static_cast<size_t>(BH) * Sq * D * 2, stream) == cudaSuccess
+                   ? GFX906_B200_OK
+                   : GFX906_B200_ECUDA;
+        } else {
+          rc = launch_d512<true>(q, k, v, o, BH, Sq, Skv, scale, stream);
+        }
+      }
+    }
+  }
   t_last_error = rc;
   return rc;
 }

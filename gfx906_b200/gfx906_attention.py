@@ -99,7 +99,9 @@ def _vae_attn(q, k, v, fallback):
     """Drop-in for the VAE ``normal_attention`` ([b, c, h, w] -> same shape).
 
     Eligible calls (CUDA fp16/bf16, equal shapes, c == 512) run as one
-    [b, 1, h*w, c] attention; the rest, and any kernel error, use ``fallback``.
+    attention over the h*w positions: on the feature maps as they are (the
+    kernel's transposed layout) when h*w is a multiple of 8, else as
+    [b, 1, h*w, c]; the rest, and any kernel error, use ``fallback``.
     """
     mod = None
     if (q.is_cuda and q.dtype in (torch.float16, torch.bfloat16)
@@ -117,13 +119,20 @@ def _vae_attn(q, k, v, fallback):
     def to_seq(t):  # [b, c, h, w] -> [b, 1, h*w, c] (a strided view)
         return t.reshape(b, c, h * w).transpose(1, 2).unsqueeze(1)
 
+    # The feature maps are already the kernel's transposed layout [b, 1, c, h*w]
+    # (sequence innermost): no transpose in or out when h*w % 8 == 0.
+    dmajor = getattr(mod, "attn_dmajor", None) if (h * w) % 8 == 0 else None
     try:
-        out = mod.attn(to_seq(qt), to_seq(kt), to_seq(vt), c ** -0.5)
+        if dmajor is not None:
+            out = dmajor(qt.reshape(b, 1, c, h * w), kt.reshape(b, 1, c, h * w),
+                         vt.reshape(b, 1, c, h * w), c ** -0.5).reshape(b, c, h, w)
+        else:
+            out = mod.attn(to_seq(qt), to_seq(kt), to_seq(vt), c ** -0.5)
+            out = out.squeeze(1).transpose(1, 2).reshape(b, c, h, w)
     except Exception:  # noqa: BLE001 - never take down a VAE decode
         logger.warning("sm_100 VAE attention failed; using %s",
                        getattr(fallback, "__name__", fallback))
         return fallback(q, k, v)
-    out = out.squeeze(1).transpose(1, 2).reshape(b, c, h, w)
     if out_dtype != torch.float16:
         out = out.to(out_dtype)
     return out

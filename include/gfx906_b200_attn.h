@@ -92,6 +92,18 @@ GFX906_B200_API int gfx906_b200_attn_launch_noalloc(const void* q, const void* k
                                     void* o, int B, int H, int Sq, int Skv, int D,
                                     float scale, cudaStream_t stream);
 
+/* Same attention with every (batch, head) matrix stored transposed: q and o
+ * are [B, H, D, Sq], k and v [B, H, D, Skv], contiguous, the sequence
+ * innermost. A [b, c, h, w] feature map is this layout with H = 1, D = c and
+ * S = h * w, so the VAE mid-block attention (deploy/gfx906_attention.py:82-111
+ * in the reference, which transposes to [b, 1, h*w, c] and back around
+ * launch) runs on the feature maps as they are. D must be 512
+ * (GFX906_B200_EHEADDIM otherwise); Sq and Skv must be multiples of 8 so that
+ * every row starts on 16 bytes (GFX906_B200_EALIGN otherwise). */
+GFX906_B200_API int gfx906_b200_attn_launch_dmajor(const void* q, const void* k, const void* v,
+                                   void* o, int B, int H, int Sq, int Skv, int D,
+                                   float scale, cudaStream_t stream);
+
 /* Size in bytes of the scratch array behind gfx906_b200_attn_launch_noalloc.
  * No counterpart in the reference. */
 GFX906_B200_API size_t gfx906_b200_attn_noalloc_capacity(void);

@@ -222,6 +222,36 @@ def test_vae_eligible_layout_and_scale(monkeypatch):
     assert attention._vae_attn(small, small, small, lambda *a: "fallback") == "fallback"
 
 
+def test_vae_feature_maps_use_the_transposed_layout(monkeypatch):
+    """h*w % 8 == 0: the [b, c, h, w] maps go to attn_dmajor as [b, 1, c, h*w] views
+    (no transpose on the way in or out); the result matches SDPA on [b, 1, h*w, c]."""
+    calls = []
+
+    def attn_dmajor(q, k, v, scale):
+        calls.append((q.dtype, tuple(q.shape), scale, q.is_contiguous()))
+        t = lambda x: x.float().transpose(2, 3)  # noqa: E731  [B,H,D,S] -> [B,H,S,D]
+        return F.scaled_dot_product_attention(t(q), t(k), t(v), scale=scale).transpose(2, 3).half()
+
+    mod = types.SimpleNamespace(attn=mock.Mock(side_effect=AssertionError("row-major path used")),
+                                attn_dmajor=attn_dmajor)
+    monkeypatch.setattr(attention.gfx906_attn, "load_attention", lambda: mod)
+    g = torch.Generator().manual_seed(2)
+    b, c, h, w = 2, 512, 4, 6
+
+    class Cuda(torch.Tensor):
+        @property
+        def is_cuda(self):
+            return True
+
+    q, k, v = (torch.randn(b, c, h, w, generator=g).half().as_subclass(Cuda) for _ in range(3))
+    out = attention._vae_attn(q, k, v, lambda *a: "fallback")
+    assert calls == [(torch.float16, (b, 1, c, h * w), c ** -0.5, True)]
+    seq = lambda t: t.float().reshape(b, c, h * w).transpose(1, 2).unsqueeze(1)  # noqa: E731
+    ref = F.scaled_dot_product_attention(seq(q), seq(k), seq(v), scale=c ** -0.5)
+    ref = ref.squeeze(1).transpose(1, 2).reshape(b, c, h, w)
+    assert out.shape == (b, c, h, w) and torch.allclose(out.float(), ref, atol=2e-3)
+
+
 # ---- install() --------------------------------------------------------------
 
 def fake_attention_module(container=None):
