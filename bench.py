@@ -61,6 +61,8 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--layout", default="rows", choices=["rows", "dmajor"],
+                    help="dmajor: D=512 configs on transposed [B,H,D,S] tensors (VAE feature maps)")
     ap.add_argument("--shard", default="heads", choices=["heads", "rows"],
                     help="heads: every rank its own batch of (batch x head) units (weak scaling); "
                          "rows: one problem, query rows split over ranks, K/V broadcast (strong scaling)")
@@ -328,7 +330,11 @@ def run_ours(args, rank, world, local):
         # same values, distinct buffers (the kernel's time does not depend on values)
         sets.append((q0.to(dev), k0.to(dev), v0.to(dev)))
     outs = [torch.empty_like(s[0]) for s in sets]
-    lib_launch = _c_launcher()
+    dmajor = args.layout == "dmajor"
+    if dmajor and cfg.D != 512:
+        raise SystemExit("--layout dmajor needs a D=512 config (C4)")
+    # d-major: the same buffers read as [B,H,D,S] (values do not change the timing)
+    lib_launch = _c_launcher(dmajor)
     stream = torch.cuda.current_stream(dev)
 
     def step(i):
@@ -372,6 +378,13 @@ def run_ours(args, rank, world, local):
     e2e_steps = max(1, args.e2e_steps)
 
     def e2e_step():
+        if dmajor:  # public transposed-layout operator, copies in and out each step
+            shp = (cfg.B, cfg.H, cfg.D, cfg.Sq)
+            o = gfx906_b200.attn_dmajor(hq.view(shp).to(dev, non_blocking=True),
+                                        hk.view(cfg.B, cfg.H, cfg.D, cfg.Skv).to(dev, non_blocking=True),
+                                        hv.view(cfg.B, cfg.H, cfg.D, cfg.Skv).to(dev, non_blocking=True), scale)
+            hout.view(shp).copy_(o, non_blocking=True)
+            return
         # public host-memory entry point: every step uploads q, k, v and downloads
         # o; blocks of (batch x head) units overlap upload, kernel and download
         gfx906_b200.attn_host(hq, hk, hv, scale, out=hout, non_blocking=True)
@@ -404,7 +417,8 @@ def run_ours(args, rank, world, local):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic",
         "config": {
-            "workload": f"{base.name}: {base.describe()}",
+            "workload": f"{base.name}: {base.describe()}" + (
+                "; tensors stored transposed [B,H,D,S] (VAE feature-map layout)" if dmajor else ""),
             "per_rank": f"each rank its own B*H={cfg.B * cfg.H} heads (weak scaling over (batch x head))",
             "l2": f"inputs rotate over {nsets} distinct sets ({nsets * set_bytes / 2**20:.0f} MiB > 126 MB L2)",
             "parallelism": f"shard (batch x head) over {world} GPU(s), no collective on the data path",
@@ -415,7 +429,8 @@ def run_ours(args, rank, world, local):
             "peak_source": f"{peak_kind} bf16 dense burst (MEASURED_PEAKS.json bf16_tflops)",
             "traffic": traffic,
             "algorithmic_bytes": cfg.io_bytes,
-            "kernel": f"attn_fwd_kernel<{128 if cfg.D == 128 else 64}>" if cfg.D <= 128 else "attn_fwd_d512",
+            "kernel": f"attn_fwd_kernel<{128 if cfg.D == 128 else 64}>" if cfg.D <= 128
+            else f"attn_fwd_d512_kernel<{'true' if dmajor else 'false'}>",
         },
         "clocks": clocks,
         "gpu_launches": args.steps * _launches_per_call(cfg),
@@ -432,9 +447,10 @@ def _launches_per_call(cfg: AttnConfig) -> int:
     return 1
 
 
-def _c_launcher():
+def _c_launcher(dmajor: bool = False):
     """Direct C-ABI launch on preallocated outputs and workspace (no allocation
-    in the timed loop): the split schedule the torch op uses."""
+    in the timed loop): the split schedule the torch op uses. dmajor: the
+    transposed-layout entry point (D=512)."""
     from gfx906_b200 import build
     from gfx906_b200.cabi import CABI
 
@@ -442,6 +458,9 @@ def _c_launcher():
     cache = {}
 
     def launch(q, k, v, o, cfg, scale, stream):
+        if dmajor:
+            return lib.launch_dmajor_status(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), cfg.B, cfg.H,
+                                            cfg.Sq, cfg.Skv, cfg.D, scale, stream.cuda_stream)
         n = lib.workspace_size(cfg.B, cfg.H, cfg.Sq, cfg.Skv, cfg.D)
         ws = cache.get(q.device)
         if n and (ws is None or ws.numel() < n):
