@@ -11,6 +11,10 @@ as the north star of this build describes them:
   kernel query blocks, one per rank, and K/V -- held by one source rank -- are
   replicated to every rank with one NCCL broadcast each before the kernel runs.
 
+``attention_sharded`` picks between the two for q, k, v held on every rank:
+(batch x head) blocks while every rank gets at least one unit, query-row
+blocks otherwise (C4's 4 heads on 8 GPUs).
+
 Optionally the output blocks are all-gathered. Collectives happen only before
 and after the local kernel call (``torch.distributed`` over NCCL on GPUs; the
 same code runs over gloo on CPU in the tests). The local compute is
@@ -106,13 +110,14 @@ def attention_by_heads(q, k, v, scale, group=None, gather=True,
     return _gather_dim(out, counts, 0, group).reshape(B, H, Sq, D)
 
 
-def attention_by_rows(q_rows, k, v, scale, Sq: int, src: int = 0, group=None, gather=True,
+def attention_by_rows(q_rows, k, v, scale, Sq: int, src: Optional[int] = 0, group=None, gather=True,
                       local_attn: Optional[Callable] = None):
     """Query-row sharding with K/V replicated from rank `src`.
 
     q_rows: this rank's query rows [B, H, rows, D] (its `row_shard` of Sq).
     k, v: full [B, H, Skv, D] on rank `src`; on other ranks tensors of the
-    same shape and dtype that receive the broadcast.
+    same shape and dtype that receive the broadcast. src=None: every rank
+    already holds k and v (no broadcast).
     Returns the full [B, H, Sq, D] output if `gather`, else this rank's rows.
     """
     attn = local_attn or _default_attn()
@@ -120,7 +125,7 @@ def attention_by_rows(q_rows, k, v, scale, Sq: int, src: int = 0, group=None, ga
     sh = row_shard(Sq, rank, world)
     if q_rows.shape[2] != sh.size:
         raise ValueError(f"rank {rank} holds {q_rows.shape[2]} query rows, its shard is {sh.size}")
-    if world > 1:
+    if world > 1 and src is not None:
         dist.broadcast(k, src=src, group=group)
         dist.broadcast(v, src=src, group=group)
     out = attn(q_rows, k, v, scale) if sh.size > 0 else q_rows.new_zeros(q_rows.shape)
@@ -128,3 +133,28 @@ def attention_by_rows(q_rows, k, v, scale, Sq: int, src: int = 0, group=None, ga
         return out
     counts = [row_shard(Sq, r, world).size for r in range(world)]
     return _gather_dim(out, counts, 2, group)
+
+
+def choose_partition(B: int, H: int, world: int) -> str:
+    """"heads" while every rank gets at least one (batch x head) unit, else "rows"."""
+    return "heads" if B * H >= world else "rows"
+
+
+def attention_sharded(q, k, v, scale, group=None, gather=True, partition: str = "auto",
+                      local_attn: Optional[Callable] = None):
+    """q, k, v: full [B, H, S, D] tensors on every rank. Each rank computes its
+    block of (batch x head) units, or -- with fewer units than ranks, or
+    partition="rows" -- its block of whole 256-row query blocks against the
+    full K/V it already holds (no broadcast). Returns the full output if
+    `gather`, else this rank's block ([units, Sq, D] or [B, H, rows, D])."""
+    world, rank = _group_world(group)
+    B, H, Sq, _ = q.shape
+    if partition == "auto":
+        partition = choose_partition(B, H, world)
+    if partition == "heads":
+        return attention_by_heads(q, k, v, scale, group=group, gather=gather, local_attn=local_attn)
+    if partition != "rows":
+        raise ValueError(f"unknown partition {partition!r}")
+    sh = row_shard(Sq, rank, world)
+    return attention_by_rows(q[:, :, sh.start:sh.stop].contiguous(), k, v, scale, Sq, src=None, group=group,
+                             gather=gather, local_attn=local_attn)

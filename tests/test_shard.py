@@ -50,11 +50,14 @@ def _worker(rank, world, port, mode, result_q):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        B, H, Sq, Skv, D = (2, 3, 300, 257, 64) if mode == "heads" else (1, 1, 1100, 700, 64)
+        B, H, Sq, Skv, D = {"heads": (2, 3, 300, 257, 64), "rows": (1, 1, 1100, 700, 64),
+                            "auto": (1, 2, 800, 300, 32)}[mode]
         q, k, v = make_qkv(B, H, Sq, Skv, D, seed=7)
         scale = D ** -0.5
         if mode == "heads":
             out = shard.attention_by_heads(q, k, v, scale, local_attn=oracle_attn)
+        elif mode == "auto":  # 2 units: heads on 2 ranks, query rows on 3
+            out = shard.attention_sharded(q, k, v, scale, local_attn=oracle_attn)
         else:
             sh = shard.row_shard(Sq, rank, world)
             q_rows = q[:, :, sh.start:sh.stop].contiguous()
@@ -69,7 +72,8 @@ def _worker(rank, world, port, mode, result_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode,world", [("heads", 2), ("rows", 2), ("rows", 3), ("heads", 3)])
+@pytest.mark.parametrize("mode,world", [("heads", 2), ("rows", 2), ("rows", 3), ("heads", 3), ("auto", 2),
+                                        ("auto", 3)])
 def test_sharded_attention_matches_unsharded(mode, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -83,3 +87,14 @@ def test_single_process_needs_no_process_group():
     ref = oracle_attn(q, k, v, 0.125)
     assert torch.equal(shard.attention_by_heads(q, k, v, 0.125, local_attn=oracle_attn), ref)
     assert torch.equal(shard.attention_by_rows(q, k, v, 0.125, 300, local_attn=oracle_attn), ref)
+
+
+def test_choose_partition():
+    assert shard.choose_partition(1, 4, 8) == "rows"   # C4 on 8 GPUs
+    assert shard.choose_partition(1, 24, 8) == "heads"  # C2 on 8 GPUs
+    assert shard.choose_partition(1, 1, 1) == "heads"
+    q, k, v = make_qkv(1, 2, 300, 200, 64, seed=8)
+    ref = oracle_attn(q, k, v, 0.125)
+    assert torch.equal(shard.attention_sharded(q, k, v, 0.125, partition="rows", local_attn=oracle_attn), ref)
+    with pytest.raises(ValueError):
+        shard.attention_sharded(q, k, v, 0.125, partition="cols", local_attn=oracle_attn)
