@@ -497,12 +497,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint64_t dQ = sdesc_sw128(sQ, 16, 1024);
       const uint64_t dK = sdesc_sw128(sKV, 16, 1024);            // K-major K tiles
       const uint64_t dV = sdesc_sw128(sKV, CHUNK_BYTES, 1024);   // MN-major V tiles
+      // k-steps of 16 head dims: 32 bytes apart inside a 64-column chunk, chunks
+      // CHUNK_BYTES apart; issued four at a time (one chunk per group).
       auto issue_qk = [&](uint32_t d_tmem, uint64_t dq, uint32_t kv_off) {
+        const uint64_t kb = dK + (kv_off >> 4);
+        if (DP == 128 || ksteps == 4) {
 #pragma unroll
-        for (int k = 0; k < DP / 16; ++k) {
-          const uint32_t off = static_cast<uint32_t>((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4;
-          if (DP == 128 || k < ksteps)
-            mma_f16_ss_warp(d_tmem, dq + off, dK + ((kv_off >> 4) + off), IDESC_QK, k > 0 ? 1u : 0u);
+          for (int c = 0; c < DP / 64; ++c) {
+            const uint32_t o = static_cast<uint32_t>(c * CHUNK_BYTES) >> 4;
+            mma4_ss_warp(d_tmem, dq + o, dq + o + 2, dq + o + 4, dq + o + 6, kb + o, kb + o + 2, kb + o + 4,
+                         kb + o + 6, IDESC_QK, c > 0 ? 1u : 0u);
+          }
+        } else {  // head dim below 64: only the k-steps that hold data
+#pragma unroll
+          for (int k = 0; k < DP / 16; ++k) {
+            const uint32_t off = static_cast<uint32_t>((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4;
+            if (k < ksteps) mma_f16_ss_warp(d_tmem, dq + off, kb + off, IDESC_QK, k > 0 ? 1u : 0u);
+          }
         }
       };
       // PV in two halves: keys 0-63 once the first half of P is stored
@@ -515,10 +526,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (!bwait_warp(bars, (hh ? C::B_P_FULL : C::B_P_HALF) + ptile, par, abort_flag, tmo, ROLE_MMA))
             return false;
           tc_fence_after();
-#pragma unroll
-          for (int k = 4 * hh; k < 4 * hh + 4; ++k)
-            mma_f16_ts_warp(d_tmem, p_tmem + 8 * k, dV + ((v_off + k * 2048) >> 4), idesc_pv,
-                            (acc || k > 0) ? 1u : 0u);
+          // keys 64 hh .. 64 hh + 63: P columns 32 hh .., V rows 2048 bytes per 16 keys
+          const uint64_t vb = dV + ((v_off + 4 * hh * 2048) >> 4);
+          mma4_ts_warp(d_tmem, p_tmem + 32 * hh, vb, vb + 128, vb + 256, vb + 384, idesc_pv,
+                       (acc || hh > 0) ? 1u : 0u);
         }
         return true;
       };
@@ -974,13 +985,17 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
           if (!next_slot(slot)) return false;
           const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            // DMAJOR: 16 head dims = 16 rows of 128 B; row-major: 32-byte steps in a 64-d box
-            const uint32_t qoff = DMAJOR ? static_cast<uint32_t>((8 * s + k) * 2048) >> 4
-                                         : static_cast<uint32_t>((2 * s + (k >> 2)) * CHUNK_BYTES + (k & 3) * 32) >> 4;
-            const uint32_t koff = soff + (DMAJOR ? static_cast<uint32_t>(k * 2048) >> 4
-                                                 : static_cast<uint32_t>((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4);
-            mma_f16_ss_warp(tS, dQ + qoff, dK + koff, IDESC_QK, (s > 0 || k > 0) ? 1u : 0u);
+          for (int c = 0; c < 2; ++c) {
+            // k-steps 4c .. 4c+3. DMAJOR: 16 head dims = 16 rows of 128 B (2048 B apart);
+            // row-major: 32-byte steps inside one 64-d box, boxes CHUNK_BYTES apart.
+            const uint32_t st = DMAJOR ? 128u : 2u;
+            const uint32_t qoff = DMAJOR ? static_cast<uint32_t>((8 * s + 4 * c) * 2048) >> 4
+                                         : static_cast<uint32_t>((2 * s + c) * CHUNK_BYTES) >> 4;
+            const uint32_t koff = soff + (DMAJOR ? static_cast<uint32_t>(4 * c * 2048) >> 4
+                                                 : static_cast<uint32_t>(c * CHUNK_BYTES) >> 4);
+            const uint64_t qa = dQ + qoff, kb = dK + koff;
+            mma4_ss_warp(tS, qa, qa + st, qa + 2 * st, qa + 3 * st, kb, kb + st, kb + 2 * st, kb + 3 * st, IDESC_QK,
+                         (s > 0 || c > 0) ? 1u : 0u);
           }
           tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + slot));
         }
@@ -996,10 +1011,14 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
           if (!next_slot(slot)) return false;
           const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
 #pragma unroll
-          for (int k = 0; k < BN / 16; ++k) {
-            const uint32_t voff = DMAJOR ? static_cast<uint32_t>((k >> 2) * CHUNK_BYTES + (k & 3) * 32) >> 4
-                                         : static_cast<uint32_t>(k * 2048) >> 4;
-            mma_f16_ts_warp(tO + 128 * s, tP + 8 * k, dV + soff + voff, IDESC_PV, (j > 0 || k > 0) ? 1u : 0u);
+          for (int c = 0; c < 2; ++c) {
+            // keys 64c .. 64c+63. DMAJOR (V K-major): 32-byte steps inside one 64-key
+            // box; row-major (V MN-major): 16 key rows = 2048 B apart.
+            const uint32_t st = DMAJOR ? 2u : 128u;
+            const uint64_t vb = dV + soff + (DMAJOR ? static_cast<uint32_t>(c * CHUNK_BYTES) >> 4
+                                                    : static_cast<uint32_t>(4 * c * 2048) >> 4);
+            mma4_ts_warp(tO + 128 * s, tP + 32 * c, vb, vb + st, vb + 2 * st, vb + 3 * st, IDESC_PV,
+                         (j > 0 || c > 0) ? 1u : 0u);
           }
           tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + slot));
         }
