@@ -43,7 +43,8 @@ def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=F
     kernel; pageable tensors work but their copies serialise.
     out: optional [B, H, Sq, D] fp16 CPU tensor for the result (allocated
     pinned when None). device: the CUDA device (default: the current one).
-    blocks: number of (batch x head) blocks (default min(B*H, 8)).
+    blocks: number of (batch x head) blocks (default min(B*H, 8); for D = 512
+    fewer, so that every block still fills the GPU).
     non_blocking: when False the call returns with ``out`` filled; when True it
     returns at once and the current CUDA stream is made to wait for the last
     download, so ``out`` is valid once that stream has been synchronised.
@@ -70,6 +71,15 @@ def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=F
         return out
     Skv = k.shape[2]
     nb = max(1, min(units, 8 if blocks is None else int(blocks)))
+    if blocks is None and D == 512:
+        # The D=512 kernel runs one CTA per (128-row query tile, head-dim half)
+        # and does not split key ranges: a block must bring about 1.5 waves of
+        # CTAs of its own, or cutting it up costs more kernel time than the
+        # overlap saves.
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        ctas_per_unit = 2 * ((Sq + 127) // 128)
+        min_units = -(-(3 * sms) // (2 * ctas_per_unit))
+        nb = max(1, min(nb, units // max(1, min_units)))
     qf, kf, vf, of = (t.view(units, -1, D) for t in (q, k, v, out))
 
     with torch.cuda.device(dev):
