@@ -71,6 +71,11 @@ def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=F
         return out
     Skv = k.shape[2]
     nb = max(1, min(units, 8 if blocks is None else int(blocks)))
+    if blocks is None:
+        # at least 8 MiB of copies per block: below that, launch and copy
+        # latencies cost more than the overlap saves
+        moved = 2 * D * units * (2 * Sq + 2 * Skv)
+        nb = max(1, min(nb, moved // (8 << 20)))
     if blocks is None and D == 512:
         # The D=512 kernel runs one CTA per (128-row query tile, head-dim half)
         # and does not split key ranges: a block must bring about 1.5 waves of
