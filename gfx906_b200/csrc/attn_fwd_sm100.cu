@@ -9,15 +9,19 @@
 // O / l at the end (attn_kernel.hip:497-511). The S x S score matrix is never
 // written to memory.
 //
-// The B200 design:
-//  * One CTA owns two 128-row query tiles of one (batch, head). Both are
-//    multiplied against every 128-key K/V tile, so each K/V tile is read from
-//    L2 once per 256 query rows.
-//  * A producer warp streams Q (once) and K/V tiles (in a ring of shared-memory
-//    stages) with TMA, 128-byte swizzled, completion tracked by mbarriers.
-//  * The MMA warp issues every tcgen05.mma (one elected lane): S_i = Q_i K^T
-//    (fp16 x fp16 -> fp32, both operands from shared memory) into tensor memory
-//    (TMEM), and O_i += P_i V with P_i read from TMEM and V from shared memory.
+// The B200 design (attn_fwd_kernel, head dim <= 128):
+//  * Persistent CTAs, one per SM, walk a list of units; a unit is two 128-row
+//    query tiles of one (batch, head), multiplied against every 128-key K/V
+//    tile, so each K/V tile is read from L2 once per 256 query rows. The key
+//    range of the last, partial wave of units can be split across CTAs, with
+//    the partial results combined on the GPU (SegIter, make_plan).
+//  * A producer warp streams each unit's Q and the K/V tiles (a ring of
+//    shared-memory stages, one key tile's K and V per stage) with TMA,
+//    128-byte swizzled, completion tracked by mbarriers.
+//  * The MMA warp issues every tcgen05.mma (four per elected lane): S_i =
+//    Q_i K^T (fp16 x fp16 -> fp32, both operands from shared memory) into
+//    tensor memory (TMEM), and O_i += P_i V with P_i read from TMEM and V from
+//    shared memory.
 //  * Two softmax warpgroups (one per query tile, one thread per query row =
 //    one TMEM lane) read S_i from TMEM, update m and l in fp32, write
 //    P_i = exp2(S_i * scale * log2(e) - m) as fp16 back into the S_i columns of
@@ -26,8 +30,9 @@
 //    O / l is unchanged, and P stays <= 256).
 //  * The MMA order S0(j), PV1(j-1), S1(j), PV0(j) lets softmax 0 run while the
 //    tensor core works on tile 1 and vice versa.
-//  * Epilogue: O_i / l -> fp16 -> swizzled shared memory (reusing Q_i's
-//    buffer) -> TMA store, which clips rows beyond Sq.
+//  * Epilogue: O_i / l -> fp16 stored by each thread straight from TMEM to its
+//    output row (a split piece writes unnormalised fp32 O, m and l to the
+//    workspace instead; the last piece combines them).
 //
 // TMEM columns (512 allocated): S0 [0,128), S1 [128,256), O0 [256,256+DP),
 // O1 [256+DP, 256+2*DP). P_i occupies the first 64 columns of S_i.
@@ -961,7 +966,8 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
     __syncwarp();
   } else if (warp == 5) {
     // ----------------------------------------------------------- MMA issuer
-    // Whole-warp issue loop, one elected lane per tcgen05 instruction.
+    // Whole-warp issue loop; one elected lane issues each group of four MMAs
+    // and each commit.
     {
       // Row-major: Q and K K-major, V MN-major. DMAJOR: Q and K MN-major (the
       // leading byte offset steps to the second 64-wide M / N block), V K-major.
