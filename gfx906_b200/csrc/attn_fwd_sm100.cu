@@ -30,12 +30,19 @@
 //    O / l is unchanged, and P stays <= 256).
 //  * The MMA order S0(j), PV1(j-1), S1(j), PV0(j) lets softmax 0 run while the
 //    tensor core works on tile 1 and vice versa.
+//  * D <= 64: P_i has TMEM columns of its own, and S_i(j+1) is issued as soon
+//    as the first half of P_i(j) is published (by then the softmax holds all
+//    of S_i(j) in registers), so the next S no longer waits for the PV that
+//    reads P. Per key tile: PV0(j) keys 0-63, S0(j+1), PV0(j) keys 64-127,
+//    the same for tile 1; the softmax waits for PV_i(j-1) before its first
+//    P store and O rescale.
 //  * Epilogue: O_i / l -> fp16 stored by each thread straight from TMEM to its
 //    output row (a split piece writes unnormalised fp32 O, m and l to the
 //    workspace instead; the last piece combines them).
 //
 // TMEM columns (512 allocated): S0 [0,128), S1 [128,256), O0 [256,256+DP),
-// O1 [256+DP, 256+2*DP). P_i occupies the first 64 columns of S_i.
+// O1 [256+DP, 256+2*DP). At D = 128 P_i occupies the first 64 columns of S_i;
+// at D <= 64 P0 is [384,448) and P1 [448,512).
 //
 // Every mbarrier wait is bounded (time limit from the host). A wait that runs
 // out sets a CTA-wide abort flag and the device status word, the other roles
@@ -124,6 +131,11 @@ struct Cfg {
   // tile in the MMA warp, whose issue loop is on the critical path: measured
   // 2-6% faster than separate K and V barriers).
   static constexpr int PAIRS = STAGES / 2;
+  // DP = 64 leaves 128 TMEM columns free (S0 S1 O0 O1 take 384): P then gets
+  // columns of its own, [384, 448) and [448, 512), instead of overwriting S,
+  // and the next S of a query tile no longer waits for the PV that reads P.
+  static constexpr bool SEP_P = DP == 64;
+  static constexpr uint32_t P_COL = 384;
   // barrier indices
   static constexpr int B_Q_FULL = 0;   // [2], per Q buffer
   static constexpr int B_Q_EMPTY = 2;  // [2]
@@ -133,7 +145,8 @@ struct Cfg {
   static constexpr int B_P_FULL = B_S_FULL + 2;
   static constexpr int B_P_HALF = B_P_FULL + 2;  // [2]: first half of P stored
   static constexpr int B_O_FULL = B_P_HALF + 2;
-  static constexpr int B_WG = B_O_FULL + 2;  // per-warpgroup rendezvous, 2 barriers
+  static constexpr int B_PV_DONE = B_O_FULL + 2;  // [2]: PV(j) done, P columns free (DP = 64)
+  static constexpr int B_WG = B_PV_DONE + 2;  // per-warpgroup rendezvous, 2 barriers
   static constexpr int B_DRAIN = B_WG + 2;
   static constexpr int NUM_BARS = B_DRAIN + 1;
   static constexpr int DATA_BYTES = (2 * QBUFS + STAGES) * TILE_BYTES;
@@ -247,11 +260,12 @@ __device__ __forceinline__ float row_extreme(const uint32_t* s, int nvalid, bool
 // key tile).
 // When half_bar is non-zero, the first half of P (keys 0..63) is published on
 // it as soon as it is stored (after before_half() has run), so the tensor core
-// can start on those keys while the second half is computed.
-template <bool MASK, typename BeforeHalf>
+// can start on those keys while the second half is computed. before_store()
+// runs once, after the first half's exponentials and before any of P is stored.
+template <bool MASK, typename BeforeHalf, typename BeforeStore>
 __device__ __forceinline__ void row_exp_store(const uint32_t* s, float sl2, float neg_m, int nvalid,
                                               uint32_t tS, float& sum0, float& sum1, uint32_t half_bar,
-                                              BeforeHalf&& before_half) {
+                                              BeforeHalf&& before_half, BeforeStore&& before_store) {
   const uint64_t sl2x2 = f2_pack(sl2, sl2);
   const uint64_t negm2 = f2_pack(neg_m, neg_m);
   uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
@@ -280,6 +294,7 @@ __device__ __forceinline__ void row_exp_store(const uint32_t* s, float sl2, floa
         acc0 = f2_add(acc0, f2_pack(e0, e1));
       pk[c2] = pack_half2(e0, e1);
     }
+    if (h == 0) before_store();
     tmem_st32(tS + 32 * h, pk);
     if (h == 0 && half_bar) {
       before_half();
@@ -293,6 +308,23 @@ __device__ __forceinline__ void row_exp_store(const uint32_t* s, float sl2, floa
   f2_unpack(acc1, c, d);
   sum0 = a + c;
   sum1 = b + d;
+}
+
+// Multiply this thread's TMEM row of O (DP fp32 columns at tO) by factor when
+// do_it (warp-uniform).
+template <int DP>
+__device__ __forceinline__ void rescale_rows(uint32_t tO, bool do_it, float factor) {
+  if (!do_it) return;
+#pragma unroll
+  for (int c = 0; c < DP / 16; ++c) {
+    uint32_t o[16];
+    tmem_ld16(tO + 16 * c, o);
+    tmem_wait_ld();
+    reg_fence16(o);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+    tmem_st16(tO + 16 * c, o);
+  }
 }
 
 // Persistent schedule shared by every role of attn_fwd_kernel: a CTA walks a
@@ -395,6 +427,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(bars + 8 * (C::B_P_FULL + i), BM);
       mbar_init(bars + 8 * (C::B_P_HALF + i), BM);
       mbar_init(bars + 8 * (C::B_O_FULL + i), 1);
+      mbar_init(bars + 8 * (C::B_PV_DONE + i), 1);
       mbar_init(bars + 8 * (C::B_WG + i), BM);
       last_flag[i] = 0;
     }
@@ -502,6 +535,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int ksteps = (p.D + 15) / 16;  // QK reduction steps over the head dim
       const uint32_t tS0 = tmem + 0, tS1 = tmem + 128;
       const uint32_t tO0 = tmem + 256, tO1 = tmem + 256 + DP;
+      const uint32_t tP0 = tmem + C::P_COL, tP1 = tmem + C::P_COL + 64;  // own P columns (SEP_P)
       // Descriptors are built once; an MMA step only adds its byte offset >> 4
       // to the start-address field (all tiles lie below 256 KiB of shared
       // memory, so the field never carries into the next one).
@@ -544,6 +578,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         return true;
       };
+      // One half of PV (SEP_P order): keys 64 hh .. 64 hh + 63 once that half
+      // of P is stored.
+      auto pv_half = [&](uint32_t d_tmem, uint32_t p_tmem, uint32_t v_off, bool acc, int ptile, int hh,
+                         uint32_t par) -> bool {
+        if (!bwait_warp(bars, (hh ? C::B_P_FULL : C::B_P_HALF) + ptile, par, abort_flag, tmo, ROLE_MMA))
+          return false;
+        tc_fence_after();
+        const uint64_t vb = dV + ((v_off + 4 * hh * 2048) >> 4);
+        mma4_ts_warp(d_tmem, p_tmem + 32 * hh, vb, vb + 128, vb + 256, vb + 384, idesc_pv,
+                     (acc || hh > 0) ? 1u : 0u);
+        return true;
+      };
 
       SegIter si;
       si.init(p, cta, G);
@@ -562,6 +608,63 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint64_t dQ0 = dQ + ((2 * qb) * C::TILE_BYTES >> 4);
         const uint64_t dQ1 = dQ + ((2 * qb + 1) * C::TILE_BYTES >> 4);
         tc_fence_after();
+        if constexpr (C::SEP_P) {
+          // S(j+1) of a query tile goes in right after the first half of PV(j):
+          // the first-half P barrier also means the softmax has read all of
+          // S(j) into registers, and P(j) has columns of its own. Per key
+          // tile: PV0(j) keys 0-63, S0(j+1), PV0(j) keys 64-127, then the same
+          // for query tile 1, then K(j) and V(j) are released.
+          int ps = it % C::PAIRS;
+          if (!bwait_warp(bars, C::B_KV_FULL + ps, (it / C::PAIRS) & 1, abort_flag, tmo, ROLE_MMA)) {
+            ok = false;
+            break;
+          }
+          ++it;
+          tc_fence_after();
+          issue_qk(tS0, dQ0, 2 * ps * C::TILE_BYTES);
+          tc_commit_warp(bars + 8 * (C::B_S_FULL + 0));
+          if (has1) {
+            issue_qk(tS1, dQ1, 2 * ps * C::TILE_BYTES);
+            tc_commit_warp(bars + 8 * (C::B_S_FULL + 1));
+          }
+          if (t1 - t0 == 1) tc_commit_warp(bars + 8 * (C::B_Q_EMPTY + qb));  // last S of the segment issued
+          for (int j = t0; j < t1; ++j) {
+            const bool nxt = j + 1 < t1;
+            int nps = 0;
+            if (nxt) {
+              nps = it % C::PAIRS;
+              if (!bwait_warp(bars, C::B_KV_FULL + nps, (it / C::PAIRS) & 1, abort_flag, tmo, ROLE_MMA)) {
+                ok = false;
+                break;
+              }
+              ++it;
+              tc_fence_after();
+            }
+            const uint32_t v_off = (2 * ps + 1) * C::TILE_BYTES;
+            if (!pv_half(tO0, tP0, v_off, j > t0, 0, 0, g0 & 1)) { ok = false; break; }
+            if (nxt) {
+              issue_qk(tS0, dQ0, 2 * nps * C::TILE_BYTES);
+              tc_commit_warp(bars + 8 * (C::B_S_FULL + 0));
+            }
+            if (!pv_half(tO0, tP0, v_off, j > t0, 0, 1, g0 & 1)) { ok = false; break; }
+            ++g0;
+            tc_commit_warp(bars + 8 * ((nxt ? C::B_PV_DONE : C::B_O_FULL) + 0));
+            if (has1) {
+              if (!pv_half(tO1, tP1, v_off, j > t0, 1, 0, g1 & 1)) { ok = false; break; }
+              if (nxt) {
+                issue_qk(tS1, dQ1, 2 * nps * C::TILE_BYTES);
+                tc_commit_warp(bars + 8 * (C::B_S_FULL + 1));
+              }
+              if (!pv_half(tO1, tP1, v_off, j > t0, 1, 1, g1 & 1)) { ok = false; break; }
+              ++g1;
+              tc_commit_warp(bars + 8 * ((nxt ? C::B_PV_DONE : C::B_O_FULL) + 1));
+            }
+            if (j + 2 == t1) tc_commit_warp(bars + 8 * (C::B_Q_EMPTY + qb));  // last S of the segment issued
+            tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + ps));  // K(j) and V(j) free
+            ps = nps;
+          }
+          continue;
+        }
         int prev_ps = 0;
         for (int j = t0; j < t1; ++j) {
           const int ps = it % C::PAIRS;
@@ -619,13 +722,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t tS = tmem + lane_off + ti * 128;
     const uint32_t tO = tmem + lane_off + 256 + ti * DP;
+    // where P is stored: over S, or in its own columns (SEP_P)
+    const uint32_t tP = C::SEP_P ? tmem + lane_off + C::P_COL + ti * 64 : tS;
     const float sl2 = p.scale_log2;
     const bool pos = sl2 >= 0.f;
     SegIter si;
     si.init(p, cta, G);
     int unit, t0, t1;
     bool first_seg;
-    uint32_t g = 0, oseg = 0, wsync = 0;
+    uint32_t g = 0, oseg = 0, wsync = 0, pvg = 0;
     bool ok = true;
     auto wg_sync = [&]() -> bool {
       mbar_arrive(bars + 8 * (C::B_WG + ti));
@@ -662,35 +767,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           m_run = m_new;
         }
         // Rescale this warp's O rows when any of them moved its max, before any
-        // of P is published. PV(j-1) of this tile completed before S(j) was
-        // signalled; PV(j) waits for the P barriers. 16 columns at a time: the
-        // whole score row is live here, and 32 more registers would spill
-        // (measured on B200: the spill-free form is 4-7% faster at D=128).
-        if (j > t0 && __any_sync(0xffffffffu, need)) {
-#pragma unroll
-          for (int c = 0; c < DP / 16; ++c) {
-            uint32_t o[16];
-            tmem_ld16(tO + 16 * c, o);
-            tmem_wait_ld();
-            reg_fence16(o);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
-            tmem_st16(tO + 16 * c, o);
+        // of P is published; PV(j) waits for the P barriers. 16 columns at a
+        // time: the whole score row is live here, and 32 more registers would
+        // spill (measured on B200: the spill-free form is 4-7% faster at D=128).
+        if constexpr (!C::SEP_P) rescale_rows<DP>(tO, j > t0 && __any_sync(0xffffffffu, need), factor);
+        // Over S, PV(j-1) of this tile completed before S(j) was signalled.
+        // With P in its own columns S(j) is computed while PV(j-1) may still
+        // run: wait for PV(j-1) (it reads P and accumulates O) only before
+        // the first P store, after the first half's exponentials.
+        bool pv_ok = true;
+        auto before_store = [&] {
+          if constexpr (C::SEP_P) {
+            if (j > t0) {
+              pv_ok = bwait_warp(bars, C::B_PV_DONE + ti, pvg & 1, abort_flag, tmo, role);
+              ++pvg;
+              tc_fence_after();
+              rescale_rows<DP>(tO, __any_sync(0xffffffffu, need), factor);
+            }
           }
-        }
+        };
         l_run *= factor;
         const float neg_m = -m_run;
         const uint32_t half_bar = bars + 8 * (C::B_P_HALF + ti);
         float lsum0, lsum1;
         if (full)
-          row_exp_store<false>(s, sl2, neg_m, nvalid, tS, lsum0, lsum1, half_bar, [] {});
+          row_exp_store<false>(s, sl2, neg_m, nvalid, tP, lsum0, lsum1, half_bar, [] {}, before_store);
         else
-          row_exp_store<true>(s, sl2, neg_m, nvalid, tS, lsum0, lsum1, half_bar, [] {});
+          row_exp_store<true>(s, sl2, neg_m, nvalid, tP, lsum0, lsum1, half_bar, [] {}, before_store);
         l_run += lsum0 + lsum1;
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(bars + 8 * (C::B_P_FULL + ti));
         ++g;
+        if (!pv_ok) { ok = false; break; }
       }
       if (!ok) break;
       // -------------------------------------------------- segment epilogue
@@ -1080,9 +1189,9 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
       l_run *= factor;
       float lsum0, lsum1;
       if (full)
-        row_exp_store<false>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {});
+        row_exp_store<false>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {}, [] {});
       else
-        row_exp_store<true>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {});
+        row_exp_store<true>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {}, [] {});
       l_run += lsum0 + lsum1;
       // O may only be rescaled once PV(j-1) has completed.
       if (j > 0) {
