@@ -10,6 +10,12 @@ of q, k, v and o still crosses the bus on every call.
 
 Blocks are contiguous in the flattened b * H + h index, so each block's q, k,
 v and o are single contiguous ranges of the [B, H, S, D] tensors.
+
+The device copies live in two persistent buffer sets per device, used by
+alternate calls. Events order each set's reuse (the uploads of call n + 2 wait
+for the kernels of call n, its kernels for the downloads of call n), so back
+to back calls allocate nothing and the uploads of one call follow those of the
+previous call on the link without waiting for its kernels or downloads.
 """
 
 from __future__ import annotations
@@ -22,6 +28,9 @@ __all__ = ["attn_host"]
 
 _streams = {}
 _streams_lock = threading.Lock()
+_pools = {}  # device index -> _Pool
+# Buffer sets larger than this are allocated per call instead of kept.
+_POOL_MAX_BYTES = 2 << 30
 
 
 def _side_streams(device: torch.device):
@@ -33,6 +42,42 @@ def _side_streams(device: torch.device):
             pair = (torch.cuda.Stream(device=device), torch.cuda.Stream(device=device))
             _streams[key] = pair
     return pair
+
+
+class _BufferSet:
+    """Device copies of q, k, v and o for one call, and the events that say
+    when the previous call using them no longer needs them."""
+
+    def __init__(self, units, Sq, Skv, D, dev):
+        self.q = torch.empty((units, Sq, D), dtype=torch.float16, device=dev)
+        self.k = torch.empty((units, Skv, D), dtype=torch.float16, device=dev)
+        self.v = torch.empty((units, Skv, D), dtype=torch.float16, device=dev)
+        self.o = torch.empty((units, Sq, D), dtype=torch.float16, device=dev)
+        self.kernels_done = None   # compute-stream event after the last kernel reading q, k, v
+        self.download_done = None  # download-stream event after the last copy out of o
+
+    def release(self, streams):
+        # the side streams may still use these buffers: the caching allocator
+        # must not hand them out before those streams get past this point
+        for t in (self.q, self.k, self.v, self.o):
+            for st in streams:
+                t.record_stream(st)
+
+
+class _Pool:
+    def __init__(self, key, dev):
+        self.key = key
+        self.sets = [_BufferSet(*key[1:], dev), _BufferSet(*key[1:], dev)]
+        self.next = 0
+        self.lock = threading.Lock()  # one call enqueues on a device at a time
+        self.compute_streams = set()  # every stream that ran kernels on these buffers
+        self.retired = False
+
+    def retire(self, side_streams):
+        # called with self.lock held, when another shape replaces this pool
+        self.retired = True
+        for bs in self.sets:
+            bs.release(tuple(side_streams) + tuple(self.compute_streams))
 
 
 def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=False):
@@ -49,7 +94,7 @@ def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=F
     returns at once and the current CUDA stream is made to wait for the last
     download, so ``out`` is valid once that stream has been synchronised.
     """
-    from . import attn  # the strict operator: raises if the native code is missing
+    from . import _module_or_raise
 
     for name, t in (("q", q), ("k", k), ("v", v)):
         if t.is_cuda:
@@ -86,41 +131,65 @@ def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=F
         min_units = -(-(3 * sms) // (2 * ctas_per_unit))
         nb = max(1, min(nb, units // max(1, min_units)))
     qf, kf, vf, of = (t.view(units, -1, D) for t in (q, k, v, out))
+    mod = _module_or_raise()  # the strict operator: raises if the native code is missing
 
     with torch.cuda.device(dev):
         compute = torch.cuda.current_stream(dev)
         up, down = _side_streams(dev)
-        # The device buffers are allocated on the compute stream; the side
-        # streams are recorded on them so that the caching allocator does not
-        # hand them out again before the copies queued there have finished.
-        dq = torch.empty((units, Sq, D), dtype=q.dtype, device=dev)
-        dk = torch.empty((units, Skv, D), dtype=q.dtype, device=dev)
-        dv = torch.empty((units, Skv, D), dtype=q.dtype, device=dev)
-        up.wait_stream(compute)  # the buffers' previous users, if any, are done
-        done = None
-        for i in range(nb):
-            lo, hi = units * i // nb, units * (i + 1) // nb
-            if hi == lo:
-                continue
-            with torch.cuda.stream(up):
-                dq[lo:hi].copy_(qf[lo:hi], non_blocking=True)
-                dk[lo:hi].copy_(kf[lo:hi], non_blocking=True)
-                dv[lo:hi].copy_(vf[lo:hi], non_blocking=True)
-                uploaded = torch.cuda.Event()
-                uploaded.record(up)
-            compute.wait_event(uploaded)
-            o = attn(dq[lo:hi].unsqueeze(0), dk[lo:hi].unsqueeze(0), dv[lo:hi].unsqueeze(0), scale)
-            computed = torch.cuda.Event()
-            computed.record(compute)
-            with torch.cuda.stream(down):
-                down.wait_event(computed)
-                of[lo:hi].copy_(o.squeeze(0), non_blocking=True)
-                o.record_stream(down)
-                done = torch.cuda.Event()
-                done.record(down)
-        for t in (dq, dk, dv):
-            t.record_stream(up)
-        compute.wait_event(done)
-        if not non_blocking:
-            done.synchronize()
+        key = (dev.index, units, Sq, Skv, D)
+        if 2 * D * units * (2 * Sq + 2 * Skv) > _POOL_MAX_BYTES:
+            pool, lock = None, threading.Lock()
+        else:
+            with _streams_lock:
+                pool = _pools.get(dev.index)
+                if pool is None or pool.key != key:
+                    if pool is not None:
+                        with pool.lock:
+                            pool.retire((up, down))
+                    pool = _Pool(key, dev)
+                    _pools[dev.index] = pool
+            lock = pool.lock
+        with lock:
+            if pool is not None and pool.retired:  # replaced by another thread meanwhile
+                pool = None
+            if pool is None:
+                bs = _BufferSet(units, Sq, Skv, D, dev)
+                up.wait_stream(compute)  # freshly allocated on the compute stream
+            else:
+                bs = pool.sets[pool.next]
+                pool.next ^= 1
+                pool.compute_streams.add(compute)
+                if bs.kernels_done is not None:
+                    up.wait_event(bs.kernels_done)
+                if bs.download_done is not None:
+                    compute.wait_event(bs.download_done)
+            done = None
+            for i in range(nb):
+                lo, hi = units * i // nb, units * (i + 1) // nb
+                if hi == lo:
+                    continue
+                with torch.cuda.stream(up):
+                    bs.q[lo:hi].copy_(qf[lo:hi], non_blocking=True)
+                    bs.k[lo:hi].copy_(kf[lo:hi], non_blocking=True)
+                    bs.v[lo:hi].copy_(vf[lo:hi], non_blocking=True)
+                    uploaded = torch.cuda.Event()
+                    uploaded.record(up)
+                compute.wait_event(uploaded)
+                mod.attn_out(bs.q[lo:hi].unsqueeze(0), bs.k[lo:hi].unsqueeze(0), bs.v[lo:hi].unsqueeze(0),
+                             scale, bs.o[lo:hi].unsqueeze(0))
+                computed = torch.cuda.Event()
+                computed.record(compute)
+                with torch.cuda.stream(down):
+                    down.wait_event(computed)
+                    of[lo:hi].copy_(bs.o[lo:hi], non_blocking=True)
+                    done = torch.cuda.Event()
+                    done.record(down)
+            bs.kernels_done = torch.cuda.Event()
+            bs.kernels_done.record(compute)
+            bs.download_done = done
+            if pool is None:
+                bs.release((up, down))
+            compute.wait_event(done)
+    if not non_blocking:
+        done.synchronize()
     return out
