@@ -36,9 +36,10 @@
 //    reads P. Per key tile: PV0(j) keys 0-63, S0(j+1), PV0(j) keys 64-127,
 //    the same for tile 1; the softmax waits for PV_i(j-1) before its first
 //    P store and O rescale.
-//  * Epilogue: O_i / l -> fp16 stored by each thread straight from TMEM to its
-//    output row (a split piece writes unnormalised fp32 O, m and l to the
-//    workspace instead; the last piece combines them).
+//  * Epilogue: O_i / l -> fp16, each warp's 32 rows staged in 4 KiB of shared
+//    memory and stored as whole 128-byte row segments (a split piece writes
+//    unnormalised fp32 O, m and l to the workspace instead; the last piece
+//    combines them and stores the same way).
 //
 // TMEM columns (512 allocated): S0 [0,128), S1 [128,256), O0 [256,256+DP),
 // O1 [256+DP, 256+2*DP). At D = 128 P_i occupies the first 64 columns of S_i;
@@ -150,7 +151,9 @@ struct Cfg {
   static constexpr int B_DRAIN = B_WG + 2;
   static constexpr int NUM_BARS = B_DRAIN + 1;
   static constexpr int DATA_BYTES = (2 * QBUFS + STAGES) * TILE_BYTES;
-  static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + DATA_BYTES + NUM_BARS * 8 + 32;
+  // Output staging: 4 KiB per softmax warp (32 rows x 64 fp16 columns).
+  static constexpr int EPI_OFF = (DATA_BYTES + NUM_BARS * 8 + 32 + 127) & ~127;
+  static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + EPI_OFF + 8 * 4096;
 };
 
 __device__ __forceinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
@@ -199,20 +202,39 @@ __device__ __forceinline__ bool bwait_warp(uint32_t bars, int idx, uint32_t pari
   return __all_sync(0xffffffffu, ok);
 }
 
-// Stores columns [c0, c0 + 32) of one output row as fp16, o[e] * inv, keeping
-// only the first D columns (D is a multiple of 8, so stores stay 16-byte).
-__device__ __forceinline__ void store_row_f16(__half* orow, int c0, int D, const uint32_t* o, float inv) {
+// Output rows through shared memory. A softmax thread owns one row of O;
+// stored straight from registers, each warp store instruction would touch 32
+// rows, i.e. 32 different 128-byte lines (measured on B200: ~5000 cycles per
+// unit for the C2 epilogue). Instead each warp writes its 32 rows x 64
+// columns as fp16 into its own 4 KiB staging tile (128-byte rows, 16-byte
+// chunks XOR-swizzled by row: conflict-free both ways), then reads it back
+// so that 8 lanes store one 128-byte row segment, 4 rows per instruction.
+// stage_32 writes columns [32 cc, 32 cc + 32) of the tile for this lane's row.
+__device__ __forceinline__ void stage_32(uint32_t stg, int lane, int cc, const uint32_t* o, float inv) {
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    if (c0 + 8 * e < D) {
-      uint4 v;
-      v.x = pack_half2(__uint_as_float(o[8 * e + 0]) * inv, __uint_as_float(o[8 * e + 1]) * inv);
-      v.y = pack_half2(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv);
-      v.z = pack_half2(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv);
-      v.w = pack_half2(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv);
-      *reinterpret_cast<uint4*>(orow + c0 + 8 * e) = v;
-    }
+    const int ch = cc * 4 + e;
+    st_shared_v4(stg + lane * 128 + ((ch ^ (lane & 7)) << 4),
+                 pack_half2(__uint_as_float(o[8 * e + 0]) * inv, __uint_as_float(o[8 * e + 1]) * inv),
+                 pack_half2(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv),
+                 pack_half2(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv),
+                 pack_half2(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv));
   }
+}
+// Stores the warp's staged tile: rows row0 .. row0 + 31 (of Sq) of matrix
+// base, columns [c0, c0 + 64) (of D; D % 8 == 0).
+__device__ __forceinline__ void flush_stage(uint32_t stg, int lane, __half* base, int row0, int Sq, int D,
+                                            int c0) {
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + (lane >> 3), ch = lane & 7;
+    const uint4 v = ld_shared_v4(stg + r * 128 + ((ch ^ (r & 7)) << 4));
+    const int col = c0 + ch * 8;
+    if (row0 + r < Sq && col < D)
+      *reinterpret_cast<uint4*>(base + static_cast<long long>(row0 + r) * D + col) = v;
+  }
+  __syncwarp();
 }
 
 // Max over the valid columns of a raw score row (min when the scale is
@@ -806,19 +828,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!bwait_warp(bars, C::B_O_FULL + ti, oseg & 1, abort_flag, tmo, role)) { ok = false; break; }
       ++oseg;
       tc_fence_after();
-      const int q_row = q_row0 + ti * BM + row;
-      const bool live = q_row < p.Sq;
-      __half* orow = p.o + (static_cast<long long>(bh) * p.Sq + (live ? q_row : 0)) * p.D;
+      // Output goes through this warp's staging tile at s0 + EPI_OFF + warp * 4 KiB
+      // (rows q_row0 + ti * BM + quad * 32 + 0..31). The addresses are formed
+      // where they are used: kept in registers across the branch they made the
+      // compiler spill at D = 128.
       if (t0 == 0 && t1 == p.n_tiles) {
-        // whole unit: O / l straight to global memory
+        // whole unit: O / l to global memory through the staging tile
         const float inv = 1.f / l_run;
 #pragma unroll
-        for (int c = 0; c < DP / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + 32 * c, o);
-          tmem_wait_ld();
-          reg_fence32(o);
-          if (live) store_row_f16(orow, c * 32, p.D, o, inv);
+        for (int hf = 0; hf < DP / 64; ++hf) {
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            uint32_t o[32];
+            tmem_ld32(tO + 64 * hf + 32 * cc, o);
+            tmem_wait_ld();
+            reg_fence32(o);
+            stage_32(s0 + C::EPI_OFF + warp * 4096, lane, cc, o, inv);
+          }
+          flush_stage(s0 + C::EPI_OFF + warp * 4096, lane, p.o + static_cast<long long>(bh) * p.Sq * p.D,
+                      q_row0 + ti * BM + quad * 32, p.Sq, p.D, 64 * hf);
         }
         continue;
       }
@@ -917,7 +945,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint32_t o[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(acc[e]);
-          if (live) store_row_f16(orow, c * 32, p.D, o, inv);
+          stage_32(s0 + C::EPI_OFF + warp * 4096, lane, c & 1, o, inv);
+          if (c & 1)
+            flush_stage(s0 + C::EPI_OFF + warp * 4096, lane, p.o + static_cast<long long>(bh) * p.Sq * p.D,
+                        q_row0 + ti * BM + quad * 32, p.Sq, p.D, 64 * (c >> 1));
         }
       }
     }
