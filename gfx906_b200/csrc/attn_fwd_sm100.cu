@@ -112,7 +112,7 @@ struct Params {
   int tail_ctas;          // CTAs that share the tail's key range (split mode)
   long long total_steps;  // (n_units - tail_unit0) * n_tiles: steps of the tail
   __half* o;              // output, [B*H, Sq, D] fp16
-  float* ws_o;            // split workspace: [tail_ctas][2][2][128][DP] partial O
+  float* ws_o;            // split workspace: [tail_ctas][2][2] slots of [DP/4][128][4] partial O
   float* ws_ml;           // [tail_ctas][2][2][128][2] partial (m, l)
   unsigned long long* ws_cnt;  // [tail units][2] arrival counters: (epoch << 8) | arrivals
   unsigned long long epoch;    // unique per launch (56 bits), tags the counters
@@ -853,7 +853,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // partial piece: unnormalised O, m and l to this CTA's workspace slot
       const int which = first_seg ? 0 : 1;
       const long long slot = (static_cast<long long>(cta) * 2 + which) * 2 + ti;
-      float* wo = p.ws_o + (slot * BM + row) * DP;
+      // chunk-major slot: 4 columns of one row are 16 bytes, the 128 rows of a
+      // 4-column chunk are contiguous, so a warp's 32 rows store 512
+      // contiguous bytes per instruction (row-major, every store touched 32 lines)
+      float* wo = p.ws_o + slot * BM * DP + row * 4;
       float* wml = p.ws_ml + (slot * BM + row) * 2;
 #pragma unroll
       for (int c = 0; c < DP / 32; ++c) {
@@ -861,10 +864,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_ld32(tO + 32 * c, o);
         tmem_wait_ld();
         reg_fence32(o);
-        float4* dst = reinterpret_cast<float4*>(wo + c * 32);
 #pragma unroll
         for (int e = 0; e < 8; ++e)
-          dst[e] = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+          *reinterpret_cast<float4*>(wo + (c * 8 + e) * BM * 4) = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
                                __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
       }
       *reinterpret_cast<float2*>(wml) = make_float2(m_run, l_run);
@@ -908,7 +910,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           // range c2 starts inside this unit (its first tail segment) iff
           // floor(c2 * W / GT) >= ubase, i.e. c2 * W >= ubase * GT
           const int which2 = (static_cast<long long>(c2) * W >= ubase * GT) ? 0 : 1;
-          rbase[k] = ((static_cast<long long>(c2) * 2 + which2) * 2 + ti) * BM + row;
+          rbase[k] = ((static_cast<long long>(c2) * 2 + which2) * 2 + ti) * BM + row;  // (slot, row)
           ml[k] = (k < np) ? __ldcg(reinterpret_cast<const float2*>(p.ws_ml + rbase[k] * 2))
                            : make_float2(-INFINITY, 0.f);
         }
@@ -931,10 +933,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < MAX_PIECES; ++k) {
             if (k < np) {
-              const float4* src = reinterpret_cast<const float4*>(p.ws_o + rbase[k] * DP + c * 32);
+              // chunk-major slot (see the partial write): chunk q of this row
+              const long long sl = rbase[k] / BM;
+              const float* sbase = p.ws_o + sl * BM * DP + (rbase[k] - sl * BM) * 4;
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
-                const float4 v4 = __ldcg(src + e);
+                const float4 v4 = __ldcg(reinterpret_cast<const float4*>(sbase + (c * 8 + e) * BM * 4));
                 acc[4 * e] = fmaf(v4.x, w[k], acc[4 * e]);
                 acc[4 * e + 1] = fmaf(v4.y, w[k], acc[4 * e + 1]);
                 acc[4 * e + 2] = fmaf(v4.z, w[k], acc[4 * e + 2]);
