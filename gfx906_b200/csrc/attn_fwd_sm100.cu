@@ -1459,7 +1459,7 @@ struct Plan {
 };
 constexpr int kMinSplitSteps = 4;   // shortest key range a CTA gets in the tail
 constexpr int kMinSplitTiles = 16;      // fewer units than SMs: split units of >= 16 key tiles
-constexpr int kMinSplitTilesTail = 128; // a partial last wave: split units of >= 128 key tiles
+constexpr int kMinSplitTilesTail = 32;  // a partial last wave: split units of >= 32 key tiles
 
 bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Plan* pl) {
   pl->n_qb = (Sq + 2 * fa::BM - 1) / (2 * fa::BM);
@@ -1473,11 +1473,12 @@ bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Pla
   // Split the tail's key range over the CTAs when whole units would leave SMs
   // idle in the last wave and units are long enough to amortise writing and
   // combining partial results: >= 16 key tiles when there are fewer units than
-  // SMs, >= 128 otherwise. Measured on B200 (TFLOP/s, whole -> split):
+  // SMs, >= 32 otherwise. Measured on B200 (TFLOP/s, whole -> split):
   // 1x16384x131072 D64 (64 units) 292 -> 668; 1x131072^2 D64 (512 units,
   // 1024 key tiles) 593 -> 688; 1x32768^2 D64 (128 units) 587 -> 649;
-  // B1 H8 S8192 D128 (64 key tiles) 1069 -> 1045; B1 H24 S4096 D128 (32 key
-  // tiles) 1028 -> 969.
+  // with the partial O stored chunk-major, B1 H8 S8192 D128 (64 key tiles)
+  // 1072 -> 1150, B1 H24 S4096 D128 (32 key tiles) 1130 -> 1162, and
+  // B2 H16 Sq4096 Skv1024 D128 (8 key tiles) 964 -> 935, which stays whole.
   const bool long_units = pl->n_tiles >= (waves == 0 ? kMinSplitTiles : kMinSplitTilesTail);
   pl->split = (allow_split && tail > 0 && long_units) ? 1 : 0;
   if (pl->split) {

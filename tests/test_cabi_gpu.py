@@ -69,7 +69,8 @@ def test_workspace_size_and_checks(lib):
     assert lib.workspace_size(1, 4, 1024, 0, 64) == 0
     assert lib.workspace_size(1, 4, 1024, 1024, 100) == 0
     assert lib.workspace_size(2, 16, 4096, 1024, 128) == 0  # 8 key tiles per unit: never split
-    assert lib.workspace_size(1, 24, 4096, 4096, 128) == 0  # 32 key tiles: the tail is not split
+    assert lib.workspace_size(1, 40, 2048, 2048, 128) == 0  # 16 key tiles: the partial last wave is not split
+    assert lib.workspace_size(1, 24, 4096, 4096, 128) > 0  # 32 key tiles: the partial last wave is split
     assert lib.workspace_size(1, 1, 131072, 131072, 64) > 0  # 1024 key tiles: the tail is split
     n = lib.workspace_size(1, 8, 16384, 16384, 128)  # 512 units of 128 key tiles: tail split
     assert n > 0
