@@ -7,8 +7,9 @@ per-lane head-dim slices, its cross-lane reduction and its tiled online
 softmax (TILE_N = 16) in float64, and which the reference checks against
 direct attention to 1e-5 (``model_check.py:136-153``).
 
-This script imports that model from a checkout of the reference (default
-``/root/reference``, or ``$GFX906_REFERENCE``), runs it on small seeded inputs
+This script imports that model from a checkout of the reference (by default
+a ``reference`` directory beside this repository, or ``$GFX906_REFERENCE``),
+runs it on small seeded inputs
 that are exactly representable in fp16 (odd lengths, Sq != Skv, every head-dim
 family the reference supports), and writes inputs and outputs to
 ``pair_model_cases.npz`` beside this file. The fixture is committed; the tests
@@ -46,7 +47,8 @@ CASES = [
 
 
 def load_reference_model():
-    root = Path(os.environ.get("GFX906_REFERENCE", "/root/reference"))
+    default = Path(__file__).resolve().parents[2].parent / "reference"
+    root = Path(os.environ.get("GFX906_REFERENCE", str(default)))
     path = root / "model_check.py"
     spec = importlib.util.spec_from_file_location("reference_model_check", path)
     mod = importlib.util.module_from_spec(spec)
