@@ -104,7 +104,8 @@ struct Params {
   float scale_log2; // scale * log2(e)
   unsigned long long timeout_ns;
   // persistent schedule of attn_fwd_kernel
-  int n_qb;               // 256-row query blocks per (batch, head)
+  int n_qb;               // query blocks (units) per (batch, head)
+  int unit_rows;          // query rows per unit: 256 (two query tiles) or 128 (one)
   int n_units;            // n_qb * B * H
   int n_tiles;            // 128-key tiles per unit
   int split;              // 1: whole units, then a stream-K split of the tail units
@@ -351,7 +352,8 @@ __device__ __forceinline__ void rescale_rows(uint32_t tO, bool do_it, float fact
 
 // Persistent schedule shared by every role of attn_fwd_kernel: a CTA walks a
 // list of segments (unit, first key tile, end key tile). A unit is one
-// 256-row query block of one (batch, head). CTA c first takes whole units c,
+// 256-row query block of one (batch, head) -- 128 rows (one query tile) for
+// problems too small to fill half the SMs otherwise. CTA c first takes whole units c,
 // c+G, c+2G, ... below tail_unit0 (all units in whole mode). In split mode the
 // remaining "tail" units are then shared by the first tail_ctas CTAs: CTA c
 // owns the contiguous range [c*W/tail_ctas, (c+1)*W/tail_ctas) of the tail's
@@ -485,8 +487,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       while (ok && si.next(unit, t0, t1, fs)) {
         const int bh = unit / p.n_qb;
-        const int q_row0 = (unit - bh * p.n_qb) * (2 * BM);
-        const bool has1 = (q_row0 + BM) < p.Sq;
+        const int q_row0 = (unit - bh * p.n_qb) * p.unit_rows;
+        const bool has1 = p.unit_rows == 2 * BM && (q_row0 + BM) < p.Sq;
         // Q buffer qb is free once every S MMA of the segment that last used
         // it (QBUFS segments ago) is done.
         const int qb = qseg % C::QBUFS;
@@ -622,8 +624,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       while (ok && si.next(unit, t0, t1, fs)) {
         const int bh = unit / p.n_qb;
-        const int q_row0 = (unit - bh * p.n_qb) * (2 * BM);
-        const bool has1 = (q_row0 + BM) < p.Sq;
+        const int q_row0 = (unit - bh * p.n_qb) * p.unit_rows;
+        const bool has1 = p.unit_rows == 2 * BM && (q_row0 + BM) < p.Sq;
         const int qb = qseg % C::QBUFS;
         if (!bwait_warp(bars, C::B_Q_FULL + qb, (qseg / C::QBUFS) & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
         ++qseg;
@@ -762,8 +764,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     };
     while (ok && si.next(unit, t0, t1, first_seg)) {
       const int bh = unit / p.n_qb;
-      const int q_row0 = (unit - bh * p.n_qb) * (2 * BM);
-      const bool has1 = (q_row0 + BM) < p.Sq;
+      const int q_row0 = (unit - bh * p.n_qb) * p.unit_rows;
+      const bool has1 = p.unit_rows == 2 * BM && (q_row0 + BM) < p.Sq;
       if (ti == 1 && !has1) continue;
       float m_run = -INFINITY;  // running max, already multiplied by scale*log2(e)
       float l_run = 0.f;
@@ -1455,6 +1457,7 @@ struct Plan {
   int tail_unit0 = 0;
   int tail_ctas = 0;
   int n_qb = 0, n_units = 0, n_tiles = 0;
+  int unit_rows = 2 * fa::BM;
   long long total_steps = 0;  // steps of the tail
 };
 constexpr int kMinSplitSteps = 4;   // shortest key range a CTA gets in the tail
@@ -1497,6 +1500,19 @@ bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Pla
     pl->total_steps = 0;
     pl->G = static_cast<int>(U < G ? U : G);
     if (pl->G < 1) pl->G = 1;
+    if (2 * U <= G) {
+      // Too few units for half the SMs and too short to split: one 128-row
+      // query tile per unit instead, twice the CTAs, and each CTA's chain
+      // S -> softmax -> PV runs without the second tile's turns in between
+      // (measured on B200: B1 H8 S1024 D64, 32 -> 64 units, 114 -> 130
+      // TFLOP/s, bit-identical).
+      pl->unit_rows = fa::BM;
+      pl->n_qb = (Sq + fa::BM - 1) / fa::BM;
+      pl->n_units = static_cast<int>(pl->n_qb * BH);
+      pl->tail_unit0 = pl->n_units;
+      pl->G = pl->n_units < G ? pl->n_units : static_cast<int>(G);
+      if (pl->G < 1) pl->G = 1;
+    }
   }
   return true;
 }
@@ -1528,6 +1544,7 @@ int launch_dp(const void* q, const void* k, const void* v, void* o, long long BH
   prm.scale_log2 = scale * 1.4426950408889634f;
   prm.timeout_ns = timeout_ns_from_env();
   prm.n_qb = pl.n_qb;
+  prm.unit_rows = pl.unit_rows;
   prm.n_units = pl.n_units;
   prm.n_tiles = pl.n_tiles;
   prm.split = pl.split;
