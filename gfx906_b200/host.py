@@ -15,7 +15,9 @@ The device copies live in two persistent buffer sets per device, used by
 alternate calls. Events order each set's reuse (the uploads of call n + 2 wait
 for the kernels of call n, its kernels for the downloads of call n), so back
 to back calls allocate nothing and the uploads of one call follow those of the
-previous call on the link without waiting for its kernels or downloads.
+previous call on the link without waiting for its kernels or downloads. The
+kernels run on a third stream of the library's, so the next call's kernels do
+not wait for this call's downloads either; only the caller's stream does.
 """
 
 from __future__ import annotations
@@ -34,14 +36,14 @@ _POOL_MAX_BYTES = 2 << 30
 
 
 def _side_streams(device: torch.device):
-    """One upload and one download stream per device, created on first use."""
+    """Upload, download and kernel streams of a device, created on first use."""
     key = device.index
     with _streams_lock:
-        pair = _streams.get(key)
-        if pair is None:
-            pair = (torch.cuda.Stream(device=device), torch.cuda.Stream(device=device))
-            _streams[key] = pair
-    return pair
+        trio = _streams.get(key)
+        if trio is None:
+            trio = tuple(torch.cuda.Stream(device=device) for _ in range(3))
+            _streams[key] = trio
+    return trio
 
 
 class _BufferSet:
@@ -70,14 +72,13 @@ class _Pool:
         self.sets = [_BufferSet(*key[1:], dev), _BufferSet(*key[1:], dev)]
         self.next = 0
         self.lock = threading.Lock()  # one call enqueues on a device at a time
-        self.compute_streams = set()  # every stream that ran kernels on these buffers
         self.retired = False
 
-    def retire(self, side_streams):
+    def retire(self, streams):
         # called with self.lock held, when another shape replaces this pool
         self.retired = True
         for bs in self.sets:
-            bs.release(tuple(side_streams) + tuple(self.compute_streams))
+            bs.release(streams)
 
 
 def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=False):
@@ -93,6 +94,10 @@ def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=F
     non_blocking: when False the call returns with ``out`` filled; when True it
     returns at once and the current CUDA stream is made to wait for the last
     download, so ``out`` is valid once that stream has been synchronised.
+    q, k and v must hold their final values when the call is made: the
+    uploads do not wait for work queued on the current stream (a
+    ``non_blocking`` device-to-host copy into them must be synchronised
+    first).
     """
     from . import _module_or_raise
 
@@ -137,8 +142,11 @@ def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=F
     mod = _module_or_raise()  # the strict operator: raises if the native code is missing
 
     with torch.cuda.device(dev):
-        compute = torch.cuda.current_stream(dev)
-        up, down = _side_streams(dev)
+        caller = torch.cuda.current_stream(dev)
+        # Kernels run on a stream of their own, not the caller's: the caller's
+        # stream waits for this call's last download, and on it the next
+        # call's kernels would wait for that download too.
+        up, down, compute = _side_streams(dev)
         key = (dev.index, units, Sq, Skv, D)
         if 2 * D * units * (2 * Sq + 2 * Skv) > _POOL_MAX_BYTES:
             pool, lock = None, threading.Lock()
@@ -148,20 +156,22 @@ def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=F
                 if pool is None or pool.key != key:
                     if pool is not None:
                         with pool.lock:
-                            pool.retire((up, down))
-                    pool = _Pool(key, dev)
+                            pool.retire((down, compute))
+                    # allocated on the upload stream, their first user: the
+                    # caching allocator only orders reuse on the allocating stream
+                    with torch.cuda.stream(up):
+                        pool = _Pool(key, dev)
                     _pools[dev.index] = pool
             lock = pool.lock
         with lock:
             if pool is not None and pool.retired:  # replaced by another thread meanwhile
                 pool = None
             if pool is None:
-                bs = _BufferSet(units, Sq, Skv, D, dev)
-                up.wait_stream(compute)  # freshly allocated on the compute stream
+                with torch.cuda.stream(up):
+                    bs = _BufferSet(units, Sq, Skv, D, dev)
             else:
                 bs = pool.sets[pool.next]
                 pool.next ^= 1
-                pool.compute_streams.add(compute)
                 if bs.kernels_done is not None:
                     up.wait_event(bs.kernels_done)
                 if bs.download_done is not None:
@@ -178,8 +188,9 @@ def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=F
                     uploaded = torch.cuda.Event()
                     uploaded.record(up)
                 compute.wait_event(uploaded)
-                mod.attn_out(bs.q[lo:hi].unsqueeze(0), bs.k[lo:hi].unsqueeze(0), bs.v[lo:hi].unsqueeze(0),
-                             scale, bs.o[lo:hi].unsqueeze(0))
+                with torch.cuda.stream(compute):
+                    mod.attn_out(bs.q[lo:hi].unsqueeze(0), bs.k[lo:hi].unsqueeze(0), bs.v[lo:hi].unsqueeze(0),
+                                 scale, bs.o[lo:hi].unsqueeze(0))
                 computed = torch.cuda.Event()
                 computed.record(compute)
                 with torch.cuda.stream(down):
@@ -191,8 +202,8 @@ def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=F
             bs.kernels_done.record(compute)
             bs.download_done = done
             if pool is None:
-                bs.release((up, down))
-            compute.wait_event(done)
+                bs.release((down, compute))
+            caller.wait_event(done)
     if not non_blocking:
         done.synchronize()
     return out
