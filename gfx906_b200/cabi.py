@@ -45,6 +45,8 @@ class CABI:
         d.gfx906_b200_attn_launch_noalloc.restype = _c_int
         d.gfx906_b200_attn_noalloc_capacity.argtypes = []
         d.gfx906_b200_attn_noalloc_capacity.restype = ctypes.c_size_t
+        d.gfx906_b200_attn_plan.argtypes = [_c_int] * 7 + [ctypes.POINTER(_c_int)]
+        d.gfx906_b200_attn_plan.restype = _c_int
         d.gfx906_b200_attn_flops.argtypes = [_c_int] * 5
         d.gfx906_b200_attn_flops.restype = ctypes.c_double
 
@@ -63,6 +65,16 @@ class CABI:
 
     def workspace_size(self, B, H, Sq, Skv, D) -> int:
         return self.dll.gfx906_b200_attn_workspace_size(B, H, Sq, Skv, D)
+
+    def plan(self, B, H, Sq, Skv, D, with_workspace=True, num_sms=0):
+        """(status, {"ctas", "split", "tail_ctas", "unit_rows"}) of the schedule a launch
+        would use on a GPU with num_sms SMs (0: the current device)."""
+        buf = (_c_int * 4)()
+        rc = self.dll.gfx906_b200_attn_plan(B, H, Sq, Skv, D, 1 if with_workspace else 0, num_sms, buf)
+        return rc, dict(zip(("ctas", "split", "tail_ctas", "unit_rows"), list(buf)))
+
+    def last_error(self) -> int:
+        return self.dll.gfx906_b200_attn_last_error()
 
     def error_string(self, status: int) -> str:
         return self.dll.gfx906_b200_attn_error_string(status).decode()

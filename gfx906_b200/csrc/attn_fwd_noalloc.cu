@@ -51,7 +51,12 @@ int noalloc_workspace(void** out) {
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_workspace) != cudaSuccess || !p) return GFX906_B200_ECUDA;
+    if (cudaGetSymbolAddress(&p, g_noalloc_workspace) != cudaSuccess || !p) {
+      // Consume the runtime's pending error, so that the next, unrelated
+      // launch's error check does not report it as its own.
+      (void)cudaGetLastError();
+      return GFX906_B200_ECUDA;
+    }
     g_noalloc_ptr[dev] = p;
   }
   *out = g_noalloc_ptr[dev];
@@ -59,6 +64,9 @@ int noalloc_workspace(void** out) {
 }
 
 }  // namespace
+
+// Records the status for gfx906_b200_attn_last_error() (attn_fwd_sm100.cu).
+extern "C" int gfx906_b200_internal_set_last_error(int status);
 
 extern "C" {
 
@@ -70,10 +78,12 @@ int gfx906_b200_attn_launch_noalloc(const void* q, const void* k, const void* v,
   // workspace entry then runs without scratch and reports any error itself.
   const size_t need = gfx906_b200_attn_workspace_size(B, H, Sq, Skv, D);
   if (need == 0) return gfx906_b200_attn_launch_ws(q, k, v, o, B, H, Sq, Skv, D, scale, nullptr, 0, stream);
-  if (need > kNoallocWorkspaceBytes) return GFX906_B200_ENOSPACE;
+  // The scratch a split schedule needs grows with the SM count (about 40 MB
+  // on a 148-SM B200); a device with more SMs can exceed the array.
+  if (need > kNoallocWorkspaceBytes) return gfx906_b200_internal_set_last_error(GFX906_B200_ENOSPACE);
   void* ws = nullptr;
   const int rc = noalloc_workspace(&ws);
-  if (rc != GFX906_B200_OK) return rc;
+  if (rc != GFX906_B200_OK) return gfx906_b200_internal_set_last_error(rc);
   return gfx906_b200_attn_launch_ws(q, k, v, o, B, H, Sq, Skv, D, scale, ws, kNoallocWorkspaceBytes, stream);
 }
 

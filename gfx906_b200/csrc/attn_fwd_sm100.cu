@@ -80,7 +80,7 @@ constexpr uint32_t REGS_CONTROL = 96;
 constexpr int PRODUCER_WARP = 8;
 constexpr int MMA_WARP = 9;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
-constexpr int MAX_PIECES = 4;              // most pieces one split unit is cut into
+constexpr int MAX_PIECES = 32;             // most pieces one split unit is cut into
 #ifndef ATTN_EMU_PAIRS
 #define ATTN_EMU_PAIRS 1
 #endif
@@ -901,30 +901,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (last_flag[ti]) {
         // Last piece to finish: combine every piece of this (unit, query tile)
         // from the workspace, in CTA order whoever combines (deterministic
-        // bits). One row per thread, all 128 rows in flight; per 32-column
-        // chunk the loads of every piece are issued together.
+        // bits). One row per thread, all 128 rows in flight. A unit spans up
+        // to MAX_PIECES CTA ranges, so the pieces are walked in a loop; each
+        // piece's (m, l) pair is re-read (8 bytes, from L1/L2) where it is
+        // needed instead of being held in registers for every piece.
         const int np = c_hi - c_lo + 1;  // <= MAX_PIECES (make_plan guarantees it)
-        long long rbase[MAX_PIECES];     // element offset of this row in each piece
-        float2 ml[MAX_PIECES];
-#pragma unroll
-        for (int k = 0; k < MAX_PIECES; ++k) {
+        // element offset of this row in piece k's slot: range c_lo + k starts
+        // inside this unit (its first tail segment) iff floor(c * W / GT) >=
+        // ubase, i.e. c * W >= ubase * GT
+        auto piece_row = [&](int k) -> long long {
           const int c2 = c_lo + k;
-          // range c2 starts inside this unit (its first tail segment) iff
-          // floor(c2 * W / GT) >= ubase, i.e. c2 * W >= ubase * GT
           const int which2 = (static_cast<long long>(c2) * W >= ubase * GT) ? 0 : 1;
-          rbase[k] = ((static_cast<long long>(c2) * 2 + which2) * 2 + ti) * BM + row;  // (slot, row)
-          ml[k] = (k < np) ? __ldcg(reinterpret_cast<const float2*>(p.ws_ml + rbase[k] * 2))
-                           : make_float2(-INFINITY, 0.f);
-        }
+          return ((static_cast<long long>(c2) * 2 + which2) * 2 + ti) * BM + row;  // (slot, row)
+        };
+        auto piece_ml = [&](long long rb) -> float2 {
+          return __ldcg(reinterpret_cast<const float2*>(p.ws_ml + rb * 2));
+        };
         float m_all = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < MAX_PIECES; ++k) m_all = fmaxf(m_all, ml[k].x);
-        float w[MAX_PIECES];
+#pragma unroll 1
+        for (int k = 0; k < np; ++k) m_all = fmaxf(m_all, piece_ml(piece_row(k)).x);
         float l_all = 0.f;
-#pragma unroll
-        for (int k = 0; k < MAX_PIECES; ++k) {
-          w[k] = (k < np) ? ex2_approx(ml[k].x - m_all) : 0.f;
-          l_all = fmaf(ml[k].y, w[k], l_all);
+#pragma unroll 1
+        for (int k = 0; k < np; ++k) {
+          const float2 ml = piece_ml(piece_row(k));
+          l_all = fmaf(ml.y, ex2_approx(ml.x - m_all), l_all);
         }
         const float inv = 1.f / l_all;
 #pragma unroll 1
@@ -932,20 +932,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           float acc[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+#pragma unroll 1
+          for (int k = 0; k < np; ++k) {
+            const long long rb = piece_row(k);
+            const float wk = ex2_approx(piece_ml(rb).x - m_all);
+            // chunk-major slot (see the partial write): chunk q of this row
+            const long long sl = rb / BM;
+            const float* sbase = p.ws_o + sl * BM * DP + (rb - sl * BM) * 4;
+            float4 v4[8];
 #pragma unroll
-          for (int k = 0; k < MAX_PIECES; ++k) {
-            if (k < np) {
-              // chunk-major slot (see the partial write): chunk q of this row
-              const long long sl = rbase[k] / BM;
-              const float* sbase = p.ws_o + sl * BM * DP + (rbase[k] - sl * BM) * 4;
+            for (int e = 0; e < 8; ++e) v4[e] = __ldcg(reinterpret_cast<const float4*>(sbase + (c * 8 + e) * BM * 4));
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float4 v4 = __ldcg(reinterpret_cast<const float4*>(sbase + (c * 8 + e) * BM * 4));
-                acc[4 * e] = fmaf(v4.x, w[k], acc[4 * e]);
-                acc[4 * e + 1] = fmaf(v4.y, w[k], acc[4 * e + 1]);
-                acc[4 * e + 2] = fmaf(v4.z, w[k], acc[4 * e + 2]);
-                acc[4 * e + 3] = fmaf(v4.w, w[k], acc[4 * e + 3]);
-              }
+            for (int e = 0; e < 8; ++e) {
+              acc[4 * e] = fmaf(v4[e].x, wk, acc[4 * e]);
+              acc[4 * e + 1] = fmaf(v4[e].y, wk, acc[4 * e + 1]);
+              acc[4 * e + 2] = fmaf(v4[e].z, wk, acc[4 * e + 2]);
+              acc[4 * e + 3] = fmaf(v4[e].w, wk, acc[4 * e + 3]);
             }
           }
           uint32_t o[32];
@@ -1463,34 +1465,49 @@ struct Plan {
 constexpr int kMinSplitSteps = 4;   // shortest key range a CTA gets in the tail
 constexpr int kMinSplitTiles = 16;      // fewer units than SMs: split units of >= 16 key tiles
 constexpr int kMinSplitTilesTail = 32;  // a partial last wave: split units of >= 32 key tiles
+#ifndef ATTN_MIN_SPLIT_TILES_SHORT
+#define ATTN_MIN_SPLIT_TILES_SHORT 8
+#endif
+// 128-row units (problems too small to fill half the SMs with 256-row units):
+// split units of >= this many key tiles.
+constexpr int kMinSplitTilesShort = ATTN_MIN_SPLIT_TILES_SHORT;
 
 bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Plan* pl) {
-  pl->n_qb = (Sq + 2 * fa::BM - 1) / (2 * fa::BM);
   pl->n_tiles = (Skv + fa::BN - 1) / fa::BN;
+  const long long G = num_sms;
+  const long long U256 = static_cast<long long>((Sq + 2 * fa::BM - 1) / (2 * fa::BM)) * BH;
+  // Too few 256-row units for half the SMs, and units too short to split at
+  // that size: one 128-row query tile per unit instead, twice the CTAs, and
+  // each CTA's chain S -> softmax -> PV runs without the second tile's turns
+  // in between (measured on B200: B1 H8 S1024 D64, 32 -> 64 units, 114 ->
+  // 130 TFLOP/s, bit-identical).
+  const bool short_units = 2 * U256 <= G && (!allow_split || pl->n_tiles < kMinSplitTiles);
+  pl->unit_rows = short_units ? fa::BM : 2 * fa::BM;
+  pl->n_qb = (Sq + pl->unit_rows - 1) / pl->unit_rows;
   const long long U = static_cast<long long>(pl->n_qb) * BH;
   if (U > 0x7fffffffll) return false;
   pl->n_units = static_cast<int>(U);
-  const long long G = num_sms;
   const long long waves = U / G;       // full waves of whole units
   const long long tail = U - waves * G;  // units left for a partial last wave
   // Split the tail's key range over the CTAs when whole units would leave SMs
   // idle in the last wave and units are long enough to amortise writing and
   // combining partial results: >= 16 key tiles when there are fewer units than
-  // SMs, >= 32 otherwise. Measured on B200 (TFLOP/s, whole -> split):
-  // 1x16384x131072 D64 (64 units) 292 -> 668; 1x131072^2 D64 (512 units,
-  // 1024 key tiles) 593 -> 688; 1x32768^2 D64 (128 units) 587 -> 649;
-  // with the partial O stored chunk-major, B1 H8 S8192 D128 (64 key tiles)
-  // 1072 -> 1150, B1 H24 S4096 D128 (32 key tiles) 1130 -> 1162, and
+  // SMs, >= 32 otherwise, >= 8 for 128-row units. Measured on B200 (TFLOP/s,
+  // whole -> split): 1x16384x131072 D64 (64 units) 292 -> 668; 1x131072^2 D64
+  // (512 units, 1024 key tiles) 593 -> 688; 1x32768^2 D64 (128 units) 587 ->
+  // 649; with the partial O stored chunk-major, B1 H8 S8192 D128 (64 key
+  // tiles) 1072 -> 1150, B1 H24 S4096 D128 (32 key tiles) 1130 -> 1162, and
   // B2 H16 Sq4096 Skv1024 D128 (8 key tiles) 964 -> 935, which stays whole.
-  const bool long_units = pl->n_tiles >= (waves == 0 ? kMinSplitTiles : kMinSplitTilesTail);
-  pl->split = (allow_split && tail > 0 && long_units) ? 1 : 0;
+  const int min_tiles = short_units ? kMinSplitTilesShort : (waves == 0 ? kMinSplitTiles : kMinSplitTilesTail);
+  pl->split = (allow_split && tail > 0 && pl->n_tiles >= min_tiles) ? 1 : 0;
   if (pl->split) {
     pl->tail_unit0 = static_cast<int>(waves * G);
     pl->total_steps = tail * pl->n_tiles;
     long long gt = (pl->total_steps + kMinSplitSteps - 1) / kMinSplitSteps;
     if (gt > G) gt = G;
     // every CTA range is at least tail*T/gt >= T/(MAX_PIECES-1) steps long, so a
-    // unit spans at most MAX_PIECES ranges
+    // unit spans at most about MAX_PIECES ranges (a 16-unit shard of one long
+    // head still gets all 148 SMs of a B200)
     if (gt > (fa::MAX_PIECES - 1) * tail) gt = (fa::MAX_PIECES - 1) * tail;
     pl->tail_ctas = static_cast<int>(gt);
     pl->G = static_cast<int>(waves > 0 ? G : gt);
@@ -1500,19 +1517,6 @@ bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Pla
     pl->total_steps = 0;
     pl->G = static_cast<int>(U < G ? U : G);
     if (pl->G < 1) pl->G = 1;
-    if (2 * U <= G) {
-      // Too few units for half the SMs and too short to split: one 128-row
-      // query tile per unit instead, twice the CTAs, and each CTA's chain
-      // S -> softmax -> PV runs without the second tile's turns in between
-      // (measured on B200: B1 H8 S1024 D64, 32 -> 64 units, 114 -> 130
-      // TFLOP/s, bit-identical).
-      pl->unit_rows = fa::BM;
-      pl->n_qb = (Sq + fa::BM - 1) / fa::BM;
-      pl->n_units = static_cast<int>(pl->n_qb * BH);
-      pl->tail_unit0 = pl->n_units;
-      pl->G = pl->n_units < G ? pl->n_units : static_cast<int>(G);
-      if (pl->G < 1) pl->G = 1;
-    }
   }
   return true;
 }
@@ -1690,6 +1694,41 @@ size_t gfx906_b200_attn_workspace_size(int B, int H, int Sq, int Skv, int D) {
   Plan pl;
   if (!make_plan(static_cast<long long>(B) * H, Sq, Skv, device_sms(dev), true, &pl)) return 0;
   return workspace_bytes(pl, D == 128 ? 128 : 64);
+}
+
+int gfx906_b200_attn_plan(int B, int H, int Sq, int Skv, int D, int with_workspace, int num_sms, int* out4) {
+  if (!out4) return GFX906_B200_EINVAL;
+  bool skip = false;
+  const void* fake = reinterpret_cast<const void*>(static_cast<uintptr_t>(16));
+  int rc = check_args(fake, fake, fake, fake, B, H, Sq, Skv, D, &skip);
+  if (rc != GFX906_B200_OK) return rc;
+  out4[0] = out4[1] = out4[2] = out4[3] = 0;
+  if (skip || Skv == 0) return GFX906_B200_OK;  // nothing is launched
+  if (num_sms <= 0) {
+    int dev = 0;
+    rc = check_device(&dev);
+    if (rc != GFX906_B200_OK) return rc;
+    num_sms = device_sms(dev);
+  }
+  const long long BH = static_cast<long long>(B) * H;
+  if (D == 512) {
+    const long long ctas = 2ll * ((Sq + fa::BM - 1) / fa::BM) * BH;
+    out4[0] = static_cast<int>(ctas < 0x7fffffffll ? ctas : 0x7fffffffll);
+    out4[3] = fa::BM;
+    return GFX906_B200_OK;
+  }
+  Plan pl;
+  if (!make_plan(BH, Sq, Skv, num_sms, with_workspace != 0, &pl)) return GFX906_B200_EINVAL;
+  out4[0] = pl.G;
+  out4[1] = pl.split;
+  out4[2] = pl.tail_ctas;
+  out4[3] = pl.unit_rows;
+  return GFX906_B200_OK;
+}
+
+int gfx906_b200_internal_set_last_error(int status) {
+  t_last_error = status;
+  return status;
 }
 
 int gfx906_b200_attn_launch_ws(const void* q, const void* k, const void* v, void* o, int B, int H, int Sq,

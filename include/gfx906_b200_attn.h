@@ -77,6 +77,18 @@ GFX906_B200_API int gfx906_b200_attn_launch_ws(const void* q, const void* k, con
                                float scale, void* workspace, size_t workspace_bytes,
                                cudaStream_t stream);
 
+/* Schedule that gfx906_b200_attn_launch (with_workspace == 0) or
+ * gfx906_b200_attn_launch_ws (with_workspace != 0) picks for these sizes on
+ * a GPU with num_sms SMs (num_sms <= 0: the current device, which must then
+ * be an sm_100 GPU; num_sms > 0 touches no GPU): out4[0] = CTAs launched,
+ * out4[1] = 1 when the key range is split across CTAs, out4[2] = CTAs
+ * sharing the split key range, out4[3] = query rows per work unit (128 or
+ * 256). All zero when nothing is launched (an empty problem, Skv == 0).
+ * Returns a GFX906_B200_* status. No reference counterpart: the reference's
+ * grid is always (B*H, ceil(Sq/64)) (attn_kernel.hip:714-741). */
+GFX906_B200_API int gfx906_b200_attn_plan(int B, int H, int Sq, int Skv, int D,
+                          int with_workspace, int num_sms, int* out4);
+
 /* Allocation-free form of gfx906_b200_attn_launch_ws, for callers that cannot
  * allocate device memory (a plugin whose host runtime owns all device memory,
  * an application with a fixed memory budget, a latency-critical path where
@@ -85,9 +97,11 @@ GFX906_B200_API int gfx906_b200_attn_launch_ws(const void* q, const void* k, con
  * the library; a GPU holds it from the first call on that device until the
  * process exits. That first call looks up the array's device address and
  * should come before any stream capture on the device. Calls whose split
- * schedule needs more scratch return GFX906_B200_ENOSPACE. All calls on a
- * device share the array: calls that overlap on the GPU race, so order them
- * on one stream. Allocates nothing. No counterpart in the reference. */
+ * schedule needs more scratch return GFX906_B200_ENOSPACE; the scratch a
+ * schedule needs grows with the device's SM count (at most ~40 MB on a
+ * 148-SM B200, so no call on a B200 gets ENOSPACE). All calls on a device
+ * share the array: calls that overlap on the GPU race, so order them on one
+ * stream. Allocates nothing. No counterpart in the reference. */
 GFX906_B200_API int gfx906_b200_attn_launch_noalloc(const void* q, const void* k, const void* v,
                                     void* o, int B, int H, int Sq, int Skv, int D,
                                     float scale, cudaStream_t stream);

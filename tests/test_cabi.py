@@ -72,3 +72,55 @@ def test_error_strings_and_flops(lib):
         assert s and s != "unknown status"
     assert lib.error_string(999) == "unknown status"
     assert lib.dll.gfx906_b200_attn_flops(1, 24, 4096, 4096, 128) == 4.0 * 24 * 4096 * 4096 * 128
+
+
+B200_SMS = 148
+
+
+def plan(lib, *shape, ws=True, sms=B200_SMS):
+    rc, pl = lib.plan(*shape, with_workspace=ws, num_sms=sms)
+    assert rc == STATUS["OK"], lib.error_string(rc)
+    return pl
+
+
+def test_plan_fills_a_b200_for_small_row_shards(lib):
+    """One 8-GPU rank's shard of one long head (C5 at S=32768: 4096 query rows
+    x 32768 keys, 16 units of 256 rows x 256 key tiles) gets every SM."""
+    pl = plan(lib, 1, 1, 4096, 32768, 64)
+    assert pl["split"] == 1 and pl["ctas"] == B200_SMS and pl["tail_ctas"] == B200_SMS
+    assert pl["unit_rows"] == 256
+    # C5 at S=131072 on 8 GPUs (64 units per rank) and on one GPU
+    assert plan(lib, 1, 1, 16384, 131072, 64)["ctas"] == B200_SMS
+    assert plan(lib, 1, 1, 131072, 131072, 64)["ctas"] == B200_SMS
+    # two units: at most 31 CTAs share a unit's key range
+    pl = plan(lib, 1, 1, 512, 4096, 64)
+    assert pl["split"] == 1 and pl["ctas"] <= 31 * 2
+
+
+def test_plan_short_units(lib):
+    # C1: 8 key tiles per unit, too few units for half the SMs: 128-row units
+    # whose key range is split in two (128 CTAs of 148)
+    assert plan(lib, 1, 8, 1024, 1024, 64) == {"ctas": 128, "split": 1, "tail_ctas": 128, "unit_rows": 128}
+    # without a workspace: whole 128-row units (64 CTAs)
+    assert plan(lib, 1, 8, 1024, 1024, 64, ws=False) == {"ctas": 64, "split": 0, "tail_ctas": 0, "unit_rows": 128}
+    # C3: 512 units of 8 key tiles stay whole on every SM
+    assert plan(lib, 2, 16, 4096, 1024, 128) == {"ctas": 148, "split": 0, "tail_ctas": 0, "unit_rows": 256}
+    # C2: the partial last wave of 32-key-tile units is split
+    pl = plan(lib, 1, 24, 4096, 4096, 128)
+    assert pl["split"] == 1 and pl["ctas"] == 148
+    # D=512: two head-dim halves per 128-row query tile, never split
+    assert plan(lib, 1, 4, 4096, 4096, 512) == {"ctas": 256, "split": 0, "tail_ctas": 0, "unit_rows": 128}
+
+
+def test_plan_argument_checks(lib):
+    buf = (ctypes.c_int * 4)()
+    assert lib.dll.gfx906_b200_attn_plan(1, 1, 8, 8, 64, 1, 148, None) == STATUS["EINVAL"]
+    assert lib.dll.gfx906_b200_attn_plan(1, 1, 8, 8, 100, 1, 148, buf) == STATUS["EHEADDIM"]
+    assert lib.dll.gfx906_b200_attn_plan(1, 1, 8, 0, 64, 1, 148, buf) == STATUS["OK"] and list(buf) == [0] * 4
+
+
+def test_noalloc_records_argument_errors(lib):
+    assert lib.launch_noalloc_status(None, None, None, None, 1, 1, 8, 8, 100, 0.1) == STATUS["EHEADDIM"]
+    assert lib.last_error() == STATUS["EHEADDIM"]
+    assert lib.launch_noalloc_status(None, None, None, None, 0, 1, 8, 8, 64, 0.1) == STATUS["OK"]
+    assert lib.last_error() == STATUS["OK"]
