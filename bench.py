@@ -22,6 +22,11 @@ copies all of q, k, v host->device and all of o back, inside the timed
 region; the copies of one block of (batch x head) units overlap the kernel of
 the previous block and the download of the one before.
 
+`strong` (a list in the same line) is the strong-scaling record of the
+path's multi-GPU form: C5 (and C5 at S=32768) with query rows cut over the N
+ranks, K/V broadcast from rank 0 and O all-gathered over NCCL; it gives the
+kernel-only time and the time with the collectives, both max over ranks.
+
 `--impl reference` times the reference's CPU path (fp32 SDPA MATH on the host
 cores, from the CPU oracle) on a bounded sample of the same workload.
 """
@@ -59,6 +64,9 @@ def parse_args():
     ap.add_argument("--config", default="C2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--strong-steps", type=int, default=10,
+                    help="steps of each leg of the strong-scaling record (C5, C5s rows-sharded)")
+    ap.add_argument("--no-strong", action="store_true", help="skip the strong-scaling record")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--layout", default="rows", choices=["rows", "dmajor"],
@@ -247,66 +255,93 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def run_rows(args, rank, world, local):
-    """Strong scaling of one problem: query rows split over ranks, K/V replicated
-    from rank 0 by NCCL broadcast (gfx906_b200.shard.attention_by_rows)."""
+def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, warmup: int) -> dict:
+    """Strong scaling of one problem: cfg's query rows cut over the ranks in
+    whole 256-row blocks, K and V broadcast from rank 0 with NCCL, O gathered
+    with all_gather_into_tensor (gfx906_b200.shard.attention_by_rows). Times,
+    each the max over ranks of CUDA events on the launching stream: the kernel
+    alone, the broadcast alone, the gather alone, and the three together."""
     import gfx906_b200
     from gfx906_b200 import shard
 
-    torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if gfx906_b200.load_attention() is None:
-        raise RuntimeError(f"sm_100 attention operator unavailable: {gfx906_b200.last_error()}")
-    cfg = CONFIGS[args.config]
     q, k, v = make_qkv(cfg.B, cfg.H, cfg.Sq, cfg.Skv, cfg.D, cfg.seed, cfg.std)
     sh = shard.row_shard(cfg.Sq, rank, world)
     q_rows = q[:, :, sh.start:sh.stop].contiguous().to(dev)
     kd, vd = k.to(dev), v.to(dev)
+    del q, k, v
+    out_full = torch.empty(cfg.B, cfg.H, cfg.Sq, cfg.D, dtype=torch.float16, device=dev)
     stream = torch.cuda.current_stream(dev)
-    for _ in range(max(3, args.warmup)):
-        gfx906_b200.attn(q_rows, kd, vd, cfg.scale)
-    torch.cuda.synchronize()
-    # kernel only, max over ranks
-    barrier(world)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local)
-    with sampler:
+    local_out = gfx906_b200.attn(q_rows, kd, vd, cfg.scale)
+    counts = [shard.row_shard(cfg.Sq, r, world).size for r in range(world)]
+
+    def bcast():
+        if world > 1:
+            torch.distributed.broadcast(kd, src=0)
+            torch.distributed.broadcast(vd, src=0)
+
+    def gather():
+        if world > 1:
+            shard._gather_dim(local_out, counts, 2, None, out=out_full)
+
+    legs = {
+        "kernel": lambda: gfx906_b200.attn(q_rows, kd, vd, cfg.scale),
+        "broadcast": bcast,
+        "gather": gather,
+        "with_collectives": lambda: shard.attention_by_rows(q_rows, kd, vd, cfg.scale, cfg.Sq, src=0,
+                                                            out=out_full),
+    }
+    ms = {}
+    for name, fn in legs.items():  # every rank runs the same legs in the same order
+        for _ in range(max(3, warmup)):  # NCCL's lazy set-up stays out of the timing
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
-            gfx906_b200.attn(q_rows, kd, vd, cfg.scale)
+        for _ in range(steps):
+            fn()
         e1.record(stream)
         torch.cuda.synchronize()
-    barrier(world)
-    ms = max_over_ranks(e0.elapsed_time(e1), world)
-    # broadcast + kernel + all-gather, max over ranks; untimed calls first, so
-    # that NCCL's lazy communicator and channel set-up stays out of the timing
-    steps_sh = max(1, min(args.steps, 10))
-    for _ in range(max(3, args.warmup)):
-        shard.attention_by_rows(q_rows, kd, vd, cfg.scale, cfg.Sq, src=0)
-    torch.cuda.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
-    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2.record(stream)
-    for _ in range(steps_sh):
-        shard.attention_by_rows(q_rows, kd, vd, cfg.scale, cfg.Sq, src=0)
-    e3.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    ms_sh = max_over_ranks(e2.elapsed_time(e3), world)
+        barrier(world)
+        ms[name] = max_over_ranks(e0.elapsed_time(e1), world) / steps
+    kv_bytes = 2 * kd.numel() * kd.element_size()
+    o_bytes = out_full.numel() * out_full.element_size()
+    return {
+        "workload": f"{cfg.name}: {cfg.describe()}",
+        "ranks": world, "rows_per_rank": sh.size, "steps": steps,
+        "kernel_ms": ms["kernel"], "broadcast_ms": ms["broadcast"], "gather_ms": ms["gather"],
+        "with_collectives_ms": ms["with_collectives"],
+        "value_kernel": cfg.flops / (ms["kernel"] * 1e-3) / 1e12,
+        "value_with_collectives": cfg.flops / (ms["with_collectives"] * 1e-3) / 1e12,
+        "unit": UNIT,
+        "collectives": (f"NCCL broadcast of K and V from rank 0 ({kv_bytes / 2**20:.0f} MiB) and "
+                        f"all_gather_into_tensor of O ({o_bytes / 2**20:.0f} MiB) over {world} rank(s)"
+                        if world > 1 else "none (one rank)"),
+    }
+
+
+def run_rows(args, rank, world, local):
+    """--shard rows: the strong-scaling leg alone, as the line's value."""
+    import gfx906_b200
+
+    torch.cuda.set_device(local)
+    if gfx906_b200.load_attention() is None:
+        raise RuntimeError(f"sm_100 attention operator unavailable: {gfx906_b200.last_error()}")
+    cfg = CONFIGS[args.config]
+    sampler = ClockSampler(local)
+    with sampler:
+        rec = strong_rows(cfg, rank, world, local, args.steps, args.warmup)
     if rank != 0:
         return
-    value = cfg.flops * args.steps / (ms * 1e-3) / 1e12
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": max(3, args.warmup), "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "metric": METRIC, "value": rec["value_kernel"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": rec["kernel_ms"], "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": f"{cfg.name}: {cfg.describe()}",
+        "config": {"workload": rec["workload"],
                    "parallelism": f"query rows split over {world} GPU(s) in 256-row blocks, K/V broadcast"},
-        "sharded_e2e": {"value": cfg.flops * steps_sh / (ms_sh * 1e-3) / 1e12, "unit": UNIT,
-                        "ms_per_step": ms_sh / steps_sh,
-                        "includes": "NCCL broadcast of K and V, kernel, all-gather of O"},
+        "strong": rec,
         "clocks": sampler.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -410,6 +445,13 @@ def run_ours(args, rank, world, local):
     h2d = (hq.numel() + hk.numel() + hv.numel()) * hq.element_size()
     d2h = hout.numel() * hout.element_size()
 
+    # strong scaling of the long single-head configs (query rows over the ranks,
+    # K/V broadcast, O gathered): the multi-GPU path with its collectives
+    strong = []
+    if not args.no_strong:
+        for name in ("C5", "C5s"):
+            strong.append(strong_rows(CONFIGS[name], rank, world, local, args.strong_steps, 3))
+
     if rank != 0:
         return
     peak_tf, _, peak_kind = load_peaks()
@@ -442,6 +484,8 @@ def run_ours(args, rank, world, local):
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "ms_per_step": e2e_ms / e2e_steps},
     }
+    if strong:
+        line["strong"] = strong
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(base, args.cpu_seconds)
     print(json.dumps(line), flush=True)

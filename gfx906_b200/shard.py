@@ -76,9 +76,30 @@ def _group_world(group):
     return dist.get_world_size(group), dist.get_rank(group)
 
 
-def _gather_dim(local: torch.Tensor, counts, dim: int, group) -> torch.Tensor:
-    """All-gather blocks of unequal size along `dim` (padded to the largest)."""
+def _gather_dim(local: torch.Tensor, counts, dim: int, group, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """All-gather the ranks' blocks along `dim` (block r has counts[r] entries).
+
+    Equal blocks (the usual case: C5's rows on 1/2/4/8 GPUs, C2's heads) go
+    through one ``all_gather_into_tensor`` straight into the output when `dim`
+    is the outermost dimension that is not 1, with no staging copies.
+    Otherwise the blocks are padded to the largest, gathered, and
+    concatenated. `out`, when given, receives the result (its shape must be
+    the gathered shape)."""
     world = len(counts)
+    full = list(local.shape)
+    full[dim] = sum(counts)
+    if out is not None and list(out.shape) != full:
+        raise ValueError(f"out has shape {tuple(out.shape)}, the gathered shape is {tuple(full)}")
+    outer = 1
+    for n in local.shape[:dim]:
+        outer *= n
+    if len(set(counts)) == 1 and outer == 1 and local.is_contiguous():
+        dst = out if out is not None and out.is_contiguous() else local.new_empty(full)
+        dist.all_gather_into_tensor(dst.view(-1), local.view(-1), group=group)
+        if out is not None and dst is not out:
+            out.copy_(dst)
+            return out
+        return dst
     biggest = max(counts)
     pad = list(local.shape)
     pad[dim] = biggest
@@ -86,7 +107,11 @@ def _gather_dim(local: torch.Tensor, counts, dim: int, group) -> torch.Tensor:
     buf.narrow(dim, 0, local.shape[dim]).copy_(local)
     parts = [torch.empty_like(buf) for _ in range(world)]
     dist.all_gather(parts, buf, group=group)
-    return torch.cat([p.narrow(dim, 0, c) for p, c in zip(parts, counts)], dim=dim)
+    res = torch.cat([p.narrow(dim, 0, c) for p, c in zip(parts, counts)], dim=dim)
+    if out is not None:
+        out.copy_(res)
+        return out
+    return res
 
 
 def attention_by_heads(q, k, v, scale, group=None, gather=True,
@@ -111,14 +136,15 @@ def attention_by_heads(q, k, v, scale, group=None, gather=True,
 
 
 def attention_by_rows(q_rows, k, v, scale, Sq: int, src: Optional[int] = 0, group=None, gather=True,
-                      local_attn: Optional[Callable] = None):
+                      local_attn: Optional[Callable] = None, out: Optional[torch.Tensor] = None):
     """Query-row sharding with K/V replicated from rank `src`.
 
     q_rows: this rank's query rows [B, H, rows, D] (its `row_shard` of Sq).
     k, v: full [B, H, Skv, D] on rank `src`; on other ranks tensors of the
     same shape and dtype that receive the broadcast. src=None: every rank
     already holds k and v (no broadcast).
-    Returns the full [B, H, Sq, D] output if `gather`, else this rank's rows.
+    Returns the full [B, H, Sq, D] output if `gather` (written into `out` when
+    given), else this rank's rows.
     """
     attn = local_attn or _default_attn()
     world, rank = _group_world(group)
@@ -128,11 +154,14 @@ def attention_by_rows(q_rows, k, v, scale, Sq: int, src: Optional[int] = 0, grou
     if world > 1 and src is not None:
         dist.broadcast(k, src=src, group=group)
         dist.broadcast(v, src=src, group=group)
-    out = attn(q_rows, k, v, scale) if sh.size > 0 else q_rows.new_zeros(q_rows.shape)
+    local = attn(q_rows, k, v, scale) if sh.size > 0 else q_rows.new_zeros(q_rows.shape)
     if not gather or world == 1:
-        return out
+        if out is not None and gather:
+            out.copy_(local)
+            return out
+        return local
     counts = [row_shard(Sq, r, world).size for r in range(world)]
-    return _gather_dim(out, counts, 2, group)
+    return _gather_dim(local, counts, 2, group, out=out)
 
 
 def choose_partition(B: int, H: int, world: int) -> str:

@@ -51,6 +51,7 @@ def _worker(rank, world, port, mode, result_q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         B, H, Sq, Skv, D = {"heads": (2, 3, 300, 257, 64), "rows": (1, 1, 1100, 700, 64),
+                            "rows_eq": (1, 1, 256 * world * 2, 700, 64), "rows_bh": (2, 3, 512 * world, 300, 32),
                             "auto": (1, 2, 800, 300, 32)}[mode]
         q, k, v = make_qkv(B, H, Sq, Skv, D, seed=7)
         scale = D ** -0.5
@@ -63,7 +64,11 @@ def _worker(rank, world, port, mode, result_q):
             q_rows = q[:, :, sh.start:sh.stop].contiguous()
             if rank != 0:  # only rank 0 holds K/V; the others receive them
                 k, v = torch.zeros_like(k), torch.zeros_like(v)
-            out = shard.attention_by_rows(q_rows, k, v, scale, Sq, src=0, local_attn=oracle_attn)
+            # equal shards gather straight into a preallocated output
+            dst = torch.full_like(q, float("nan")) if mode != "rows" else None
+            out = shard.attention_by_rows(q_rows, k, v, scale, Sq, src=0, local_attn=oracle_attn, out=dst)
+            if dst is not None:
+                assert out is dst
         if rank == 0:
             q, k, v = make_qkv(B, H, Sq, Skv, D, seed=7)
             ref = oracle_attn(q, k, v, scale)
@@ -73,7 +78,7 @@ def _worker(rank, world, port, mode, result_q):
 
 
 @pytest.mark.parametrize("mode,world", [("heads", 2), ("rows", 2), ("rows", 3), ("heads", 3), ("auto", 2),
-                                        ("auto", 3)])
+                                        ("auto", 3), ("rows_eq", 2), ("rows_eq", 3), ("rows_bh", 2)])
 def test_sharded_attention_matches_unsharded(mode, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
