@@ -1465,12 +1465,6 @@ struct Plan {
 constexpr int kMinSplitSteps = 4;   // shortest key range a CTA gets in the tail
 constexpr int kMinSplitTiles = 16;      // fewer units than SMs: split units of >= 16 key tiles
 constexpr int kMinSplitTilesTail = 32;  // a partial last wave: split units of >= 32 key tiles
-#ifndef ATTN_MIN_SPLIT_TILES_SHORT
-#define ATTN_MIN_SPLIT_TILES_SHORT 8
-#endif
-// 128-row units (problems too small to fill half the SMs with 256-row units):
-// split units of >= this many key tiles.
-constexpr int kMinSplitTilesShort = ATTN_MIN_SPLIT_TILES_SHORT;
 
 bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Plan* pl) {
   pl->n_tiles = (Skv + fa::BN - 1) / fa::BN;
@@ -1480,7 +1474,9 @@ bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Pla
   // that size: one 128-row query tile per unit instead, twice the CTAs, and
   // each CTA's chain S -> softmax -> PV runs without the second tile's turns
   // in between (measured on B200: B1 H8 S1024 D64, 32 -> 64 units, 114 ->
-  // 130 TFLOP/s, bit-identical).
+  // 130 TFLOP/s, bit-identical). Such units are never split: cutting C1's
+  // 8-key-tile units in two over 128 CTAs measured slower than 64 CTAs of
+  // whole units (130 vs 138 TFLOP/s).
   const bool short_units = 2 * U256 <= G && (!allow_split || pl->n_tiles < kMinSplitTiles);
   pl->unit_rows = short_units ? fa::BM : 2 * fa::BM;
   pl->n_qb = (Sq + pl->unit_rows - 1) / pl->unit_rows;
@@ -1492,14 +1488,14 @@ bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Pla
   // Split the tail's key range over the CTAs when whole units would leave SMs
   // idle in the last wave and units are long enough to amortise writing and
   // combining partial results: >= 16 key tiles when there are fewer units than
-  // SMs, >= 32 otherwise, >= 8 for 128-row units. Measured on B200 (TFLOP/s,
+  // SMs, >= 32 otherwise. Measured on B200 (TFLOP/s,
   // whole -> split): 1x16384x131072 D64 (64 units) 292 -> 668; 1x131072^2 D64
   // (512 units, 1024 key tiles) 593 -> 688; 1x32768^2 D64 (128 units) 587 ->
   // 649; with the partial O stored chunk-major, B1 H8 S8192 D128 (64 key
   // tiles) 1072 -> 1150, B1 H24 S4096 D128 (32 key tiles) 1130 -> 1162, and
   // B2 H16 Sq4096 Skv1024 D128 (8 key tiles) 964 -> 935, which stays whole.
-  const int min_tiles = short_units ? kMinSplitTilesShort : (waves == 0 ? kMinSplitTiles : kMinSplitTilesTail);
-  pl->split = (allow_split && tail > 0 && pl->n_tiles >= min_tiles) ? 1 : 0;
+  const int min_tiles = waves == 0 ? kMinSplitTiles : kMinSplitTilesTail;
+  pl->split = (allow_split && !short_units && tail > 0 && pl->n_tiles >= min_tiles) ? 1 : 0;
   if (pl->split) {
     pl->tail_unit0 = static_cast<int>(waves * G);
     pl->total_steps = tail * pl->n_tiles;
