@@ -81,8 +81,8 @@ def _container_attn(q, k, v, heads, mask=None, attn_precision=None,
         logger.info("sm_100 attention: %s %s", shape, qt.dtype)
     qt, kt, vt = q.take(), k.take(), v.take()
     scale = kwargs.get("scale")
-    if scale is None:
-        scale = qt.shape[-1] ** -0.5  # SDPA's default
+    if scale is None:  # what scaled_dot_product_attention uses without a scale
+        scale = qt.shape[-1] ** -0.5
     out_dtype = qt.dtype
     if out_dtype != torch.float16:
         qt, kt, vt = qt.half(), kt.half(), vt.half()
@@ -129,8 +129,8 @@ def _vae_attn(q, k, v, fallback):
         else:
             out = mod.attn(to_seq(qt), to_seq(kt), to_seq(vt), c ** -0.5)
             out = out.squeeze(1).transpose(1, 2).reshape(b, c, h, w)
-    except Exception:  # noqa: BLE001 - never take down a VAE decode
-        logger.warning("sm_100 VAE attention failed; using %s",
+    except Exception:  # noqa: BLE001 - a kernel error must not abort the decode
+        logger.warning("sm_100 VAE attention raised; the call goes to %s instead",
                        getattr(fallback, "__name__", fallback))
         return fallback(q, k, v)
     if out_dtype != torch.float16:
@@ -139,12 +139,15 @@ def _vae_attn(q, k, v, fallback):
 
 
 def _install_vae_hook():
-    """Wrap ``vae_attention()`` so its slice / PyTorch paths use the kernel."""
+    """Replace the ``vae_attention`` factory with one whose returned callable
+    runs eligible calls on the kernel whenever the original factory chose the
+    sliced ``normal_attention`` or ``pytorch_attention``; any other choice
+    (xformers, say) is returned untouched."""
     global _stock_normal_attention
     try:
         from comfy.ldm.modules.diffusionmodules import model as _model
-    except Exception as exc:  # noqa: BLE001 - comfy not importable
-        logger.warning("sm_100 VAE attention hook skipped: %s", exc)
+    except Exception as exc:  # noqa: BLE001 - ComfyUI is not on the import path
+        logger.warning("no VAE hook installed (ComfyUI model module unavailable: %s)", exc)
         return
     if _stock_normal_attention is not None:
         return
@@ -155,22 +158,26 @@ def _install_vae_hook():
     def factory():
         fn = orig_factory()
         if fn not in intercepted:
-            return fn  # another backend (e.g. xformers) was selected
+            return fn  # a backend this hook does not replace
         return lambda q, k, v: _vae_attn(q, k, v, fn)
 
     _model.vae_attention = factory
-    logger.info("sm_100 tiled attention installed (VAE mid-block, D=512)")
+    logger.info("VAE mid-block attention (D=512) now runs on the sm_100 kernel")
 
 
 def install():
-    """Hook ``optimized_attention.container_function`` once. No-op off sm_100."""
+    """Claim ``optimized_attention.container_function`` for this module, once.
+
+    Does nothing unless the current GPU is an sm_100 part and ComfyUI's
+    attention module imports; refuses (with a warning) when another extension
+    already owns the seam."""
     global _stock_attention
     if not gfx906_attn.is_sm100():
         return
     try:
         from comfy.ldm.modules import attention as _attn
-    except Exception as exc:  # noqa: BLE001 - comfy not importable
-        logger.warning("sm_100 attention hook skipped: %s", exc)
+    except Exception as exc:  # noqa: BLE001 - ComfyUI is not on the import path
+        logger.warning("no attention hook installed (ComfyUI attention module unavailable: %s)", exc)
         return
     opt = _attn.optimized_attention
     if _stock_attention is opt:
@@ -178,11 +185,11 @@ def install():
     if not hasattr(opt, "container_function"):
         return
     if opt.container_function is not None:
-        logger.warning("optimized_attention.container_function already set; "
-                       "sm_100 attention hook not installed")
+        logger.warning("another extension owns optimized_attention.container_function; "
+                       "leaving it in place")
         return
     _stock_attention = opt
     opt.container_function = _container_attn
-    logger.info("sm_100 tiled attention installed (DiT)")
+    logger.info("DiT attention now runs on the sm_100 kernel when eligible")
     if _VAE_HOOK:
         _install_vae_hook()
