@@ -84,9 +84,6 @@ constexpr int MAX_PIECES = 32;             // most pieces one split unit is cut 
 #ifndef ATTN_EMU_PAIRS
 #define ATTN_EMU_PAIRS 1
 #endif
-#ifndef ATTN_COLSPLIT64
-#define ATTN_COLSPLIT64 0
-#endif
 // Pairs of exponentials, out of every 4 pairs (8 columns), evaluated with the
 // FMA-pipe polynomial instead of MUFU ex2 (balances the two pipes).
 constexpr int EMU_PAIRS = ATTN_EMU_PAIRS;
@@ -151,27 +148,13 @@ struct Cfg {
   static constexpr int B_P_HALF = B_P_FULL + 2;  // [2]: first half of P stored
   static constexpr int B_O_FULL = B_P_HALF + 2;
   static constexpr int B_PV_DONE = B_O_FULL + 2;  // [2]: PV(j) done, P columns free (DP = 64)
-  static constexpr int B_WG = B_PV_DONE + 2;  // per-warpgroup (COLSPLIT: per-tile) rendezvous, 2 barriers
+  static constexpr int B_WG = B_PV_DONE + 2;  // per-warpgroup rendezvous, 2 barriers
   static constexpr int B_DRAIN = B_WG + 2;
-  static constexpr int B_S_LOADED = B_DRAIN + 1;  // [2] (COLSPLIT): both warpgroups hold S_i in registers
-  static constexpr int B_LX = B_S_LOADED + 2;     // [2] (COLSPLIT): partial row sums exchanged
-  static constexpr int NUM_BARS = B_LX + 2;
+  static constexpr int NUM_BARS = B_DRAIN + 1;
   static constexpr int DATA_BYTES = (2 * QBUFS + STAGES) * TILE_BYTES;
-  // COLSPLIT (D = 128): both softmax warpgroups work on the same query tile,
-  // warpgroup g on keys [64 g, 64 g + 64) of the score row and on O columns
-  // [64 g, 64 g + 64); the two query tiles take turns. Each tile's P is then
-  // ready in about half the time, and the tiles' exponentials never compete
-  // for MUFU, which shortens the S -> softmax -> PV -> S chain that bounds
-  // D = 128 (P overwrites S there, so the next S of a tile waits for its PV).
-  static constexpr bool COLSPLIT = DP == 128 || (DP == 64 && ATTN_COLSPLIT64);
-  // Output staging per softmax warp: 32 rows x 64 fp16 columns (4 KiB), or
-  // 32 rows x 32 columns (2 KiB) with COLSPLIT, which needs the room for the
-  // row-sum exchange buffer ([2 tiles][2 halves][128 rows] fp32).
-  static constexpr int EPI_WARP_BYTES = COLSPLIT ? 2048 : 4096;
+  // Output staging: 4 KiB per softmax warp (32 rows x 64 fp16 columns).
   static constexpr int EPI_OFF = (DATA_BYTES + NUM_BARS * 8 + 32 + 127) & ~127;
-  static constexpr int LBUF_OFF = EPI_OFF + 8 * EPI_WARP_BYTES;
-  static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + LBUF_OFF + (COLSPLIT ? 2048 : 0);
-  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+  static constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + EPI_OFF + 8 * 4096;
 };
 
 __device__ __forceinline__ bool wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
@@ -248,34 +231,6 @@ __device__ __forceinline__ void flush_stage(uint32_t stg, int lane, __half* base
   for (int i = 0; i < 8; ++i) {
     const int r = i * 4 + (lane >> 3), ch = lane & 7;
     const uint4 v = ld_shared_v4(stg + r * 128 + ((ch ^ (r & 7)) << 4));
-    const int col = c0 + ch * 8;
-    if (row0 + r < Sq && col < D)
-      *reinterpret_cast<uint4*>(base + static_cast<long long>(row0 + r) * D + col) = v;
-  }
-  __syncwarp();
-}
-
-// The same through a 2 KiB staging tile of 32 rows x 32 fp16 columns (64-byte
-// rows, 16-byte chunks XOR-swizzled by row pairs: conflict-free both ways);
-// 4 lanes store one 64-byte row segment, 8 rows per instruction.
-__device__ __forceinline__ void stage_32n(uint32_t stg, int lane, const uint32_t* o, float inv) {
-#pragma unroll
-  for (int e = 0; e < 4; ++e)
-    st_shared_v4(stg + lane * 64 + ((e ^ ((lane >> 1) & 3)) << 4),
-                 pack_half2(__uint_as_float(o[8 * e + 0]) * inv, __uint_as_float(o[8 * e + 1]) * inv),
-                 pack_half2(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv),
-                 pack_half2(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv),
-                 pack_half2(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv));
-}
-// Stores rows row0 .. row0 + 31 (of Sq), columns [c0, c0 + 32) (of D) of the
-// tile staged by stage_32n.
-__device__ __forceinline__ void flush_stage_32n(uint32_t stg, int lane, __half* base, int row0, int Sq, int D,
-                                                int c0) {
-  __syncwarp();
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = i * 8 + (lane >> 2), ch = lane & 3;
-    const uint4 v = ld_shared_v4(stg + r * 64 + ((ch ^ ((r >> 1) & 3)) << 4));
     const int col = c0 + ch * 8;
     if (row0 + r < Sq && col < D)
       *reinterpret_cast<uint4*>(base + static_cast<long long>(row0 + r) * D + col) = v;
@@ -370,44 +325,6 @@ __device__ __forceinline__ void row_exp_store(const uint32_t* s, float sl2, floa
       tc_fence_before();
       mbar_arrive(half_bar);
     }
-  }
-  float a, b, c, d;
-  f2_unpack(acc0, a, b);
-  f2_unpack(acc1, c, d);
-  sum0 = a + c;
-  sum1 = b + d;
-}
-
-// P = exp2(s * sl2 + neg_m) for 64 score columns s[0..63], as 32 packed fp16
-// pairs in pk (not stored); the fp32 row sum in two partial sums. MASK zeroes
-// columns >= nvalid. EMU_PAIRS of every 4 pairs use the FMA-pipe polynomial.
-template <bool MASK>
-__device__ __forceinline__ void row_exp64(const uint32_t* s, float sl2, float neg_m, int nvalid, uint32_t* pk,
-                                          float& sum0, float& sum1) {
-  const uint64_t sl2x2 = f2_pack(sl2, sl2);
-  const uint64_t negm2 = f2_pack(neg_m, neg_m);
-  uint64_t acc0 = f2_pack(0.f, 0.f), acc1 = acc0;
-#pragma unroll
-  for (int c2 = 0; c2 < 32; ++c2) {
-    const int c = 2 * c2;
-    const uint64_t X = f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2x2, negm2);
-    float x0, x1, e0, e1;
-    f2_unpack(X, x0, x1);
-    if ((c2 & 3) < EMU_PAIRS) {
-      exp2_poly3_x2(x0, x1, e0, e1);
-    } else {
-      e0 = ex2_approx(x0);
-      e1 = ex2_approx(x1);
-    }
-    if (MASK) {
-      e0 = (c < nvalid) ? e0 : 0.f;
-      e1 = (c + 1 < nvalid) ? e1 : 0.f;
-    }
-    if (c2 & 1)
-      acc1 = f2_add(acc1, f2_pack(e0, e1));
-    else
-      acc0 = f2_add(acc0, f2_pack(e0, e1));
-    pk[c2] = pack_half2(e0, e1);
   }
   float a, b, c, d;
   f2_unpack(acc0, a, b);
@@ -532,14 +449,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(bars + 8 * (C::B_S_FULL + i), 1);
       mbar_init(bars + 8 * (C::B_P_FULL + i), BM);
-      // COLSPLIT: P_HALF counts warpgroup 0 (first half of P stored) and
-      // warpgroup 1 (its O columns rescaled); the rendezvous spans both.
-      mbar_init(bars + 8 * (C::B_P_HALF + i), C::COLSPLIT ? 2 * BM : BM);
+      mbar_init(bars + 8 * (C::B_P_HALF + i), BM);
       mbar_init(bars + 8 * (C::B_O_FULL + i), 1);
       mbar_init(bars + 8 * (C::B_PV_DONE + i), 1);
-      mbar_init(bars + 8 * (C::B_WG + i), C::COLSPLIT ? 2 * BM : BM);
-      mbar_init(bars + 8 * (C::B_S_LOADED + i), 2 * BM);
-      mbar_init(bars + 8 * (C::B_LX + i), 2 * BM);
+      mbar_init(bars + 8 * (C::B_WG + i), BM);
       last_flag[i] = 0;
     }
     mbar_init(bars + 8 * C::B_DRAIN, 1);
@@ -826,255 +739,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp < 8) {
     // ------------------------------------------------------------ softmax
     setmaxnreg_inc<REGS_SOFTMAX>();
-    if constexpr (C::COLSPLIT) {
-      // Warpgroup g owns keys [64 g, 64 g + 64) of every score row and O
-      // columns [DP/2 g, DP/2 g + DP/2) of both query tiles; all 256 threads
-      // work on tile 0, then on tile 1. Both warpgroups load the whole S row
-      // and compute the same row max (so no exchange is needed for it); each
-      // evaluates the exponentials of its own 64 keys. The row sum is kept
-      // per warpgroup and added at the end of a segment.
-      const int g = warp >> 2;    // column half
-      const int quad = warp & 3;  // TMEM lane quadrant this warp may access
-      const int row = quad * 32 + lane;
-      const int role = g ? ROLE_SOFTMAX1 : ROLE_SOFTMAX0;
-      const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-      const float sl2 = p.scale_log2;
-      const bool pos = sl2 >= 0.f;
-      const uint32_t stg = s0 + C::EPI_OFF + warp * C::EPI_WARP_BYTES;
-      volatile float* lbuf = reinterpret_cast<volatile float*>(smem + C::LBUF_OFF);  // [2][2][128]
-      SegIter si;
-      si.init(p, cta, G);
-      int unit, t0, t1;
-      bool first_seg;
-      uint32_t gS[2] = {0u, 0u}, oseg[2] = {0u, 0u}, lx[2] = {0u, 0u}, wsync[2] = {0u, 0u}, pvg[2] = {0u, 0u};
-      bool ok = true;
-      auto tile_sync = [&](int i) -> bool {
-        mbar_arrive(bars + 8 * (C::B_WG + i));
-        const bool r = bwait_warp(bars, C::B_WG + i, wsync[i] & 1, abort_flag, tmo, role);
-        ++wsync[i];
-        return r;
-      };
-      while (ok && si.next(unit, t0, t1, first_seg)) {
-        const int bh = unit / p.n_qb;
-        const int q_row0 = (unit - bh * p.n_qb) * p.unit_rows;
-        const bool has1 = p.unit_rows == 2 * BM && (q_row0 + BM) < p.Sq;
-        const int ntile = has1 ? 2 : 1;
-        float m_run[2] = {-INFINITY, -INFINITY};  // running max, times scale*log2(e)
-        float l_run[2] = {0.f, 0.f};              // this warpgroup's part of the row sum
-        for (int j = t0; j < t1 && ok; ++j) {
-          // unrolled: the per-tile state stays in registers
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            if (i >= ntile) break;
-            const uint32_t tS = tmem + lane_off + i * 128;
-            const uint32_t tOh = tmem + lane_off + 256 + i * DP + g * (DP / 2);
-            if (!bwait_warp(bars, C::B_S_FULL + i, gS[i] & 1, abort_flag, tmo, role)) { ok = false; break; }
-            tc_fence_after();
-            uint32_t sr[BN];
-#pragma unroll
-            for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + 32 * c, sr + 32 * c);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < BN / 32; ++c) reg_fence32(sr + 32 * c);
-            if constexpr (!C::SEP_P) {
-              // P is stored over S: the other warpgroup may store its half only
-              // once this one has read all of S.
-              tc_fence_before();
-              mbar_arrive(bars + 8 * (C::B_S_LOADED + i));
-            }
-            const int nvalid = min(BN, p.Skv - j * BN);
-            const bool full = nvalid == BN;
-            const float mx = row_extreme(sr, nvalid, full, pos);
-            const float m_new = fmaxf(m_run[i], mx * sl2);
-            const bool need = m_new > m_run[i] + RESCALE_THRESHOLD;
-            float factor = 1.f;
-            if (need) {
-              factor = ex2_approx(m_run[i] - m_new);  // 0 on the first tile (m_run = -inf)
-              m_run[i] = m_new;
-            }
-            // Each warpgroup rescales its O columns before any PV_i(j) is
-            // issued (P_HALF counts both warpgroups). With P over S, PV_i(j-1)
-            // completed before S_i(j) was signalled; with P in its own columns
-            // it may still run, so PV_DONE is waited for first.
-            const bool resc = j > t0 && __any_sync(0xffffffffu, need);
-            bool pv_seen = !C::SEP_P || j == t0;
-            if constexpr (!C::SEP_P) rescale_rows<DP / 2>(tOh, resc, factor);
-            if (g == 1) {
-              if constexpr (C::SEP_P) {
-                if (resc) {
-                  if (!bwait_warp(bars, C::B_PV_DONE + i, pvg[i] & 1, abort_flag, tmo, role)) { ok = false; break; }
-                  tc_fence_after();
-                  pv_seen = true;
-                  rescale_rows<DP / 2>(tOh, true, factor);
-                }
-              }
-              tmem_wait_st();
-              tc_fence_before();
-              mbar_arrive(bars + 8 * (C::B_P_HALF + i));
-            }
-            uint32_t pk[32];
-            float ls0, ls1;
-            // (register arrays are indexed with constants only)
-            if (g == 0) {
-              if (full)
-                row_exp64<false>(sr, sl2, -m_run[i], BN, pk, ls0, ls1);
-              else
-                row_exp64<true>(sr, sl2, -m_run[i], nvalid, pk, ls0, ls1);
-            } else {
-              if (full)
-                row_exp64<false>(sr + 64, sl2, -m_run[i], BN, pk, ls0, ls1);
-              else
-                row_exp64<true>(sr + 64, sl2, -m_run[i], nvalid - 64, pk, ls0, ls1);
-            }
-            l_run[i] = l_run[i] * factor + (ls0 + ls1);
-            if constexpr (C::SEP_P) {
-              // P_i(j-1) in these columns is read by PV_i(j-1): wait for it
-              if (!pv_seen) {
-                if (!bwait_warp(bars, C::B_PV_DONE + i, pvg[i] & 1, abort_flag, tmo, role)) { ok = false; break; }
-                tc_fence_after();
-              }
-              if (j > t0) ++pvg[i];
-              if (g == 0) rescale_rows<DP / 2>(tOh, resc, factor);
-            } else {
-              if (!bwait_warp(bars, C::B_S_LOADED + i, gS[i] & 1, abort_flag, tmo, role)) { ok = false; break; }
-              tc_fence_after();
-            }
-            // keys 64 g .. 64 g + 63 as fp16 pairs, over S or in P's own columns
-            tmem_st32((C::SEP_P ? tmem + lane_off + C::P_COL + i * 64 : tS) + 32 * g, pk);
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(bars + 8 * ((g ? C::B_P_FULL : C::B_P_HALF) + i));
-            ++gS[i];
-          }
-        }
-        if (!ok) break;
-        // ------------------------------------------------ segment epilogue
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          if (i >= ntile || !ok) break;
-          if (!bwait_warp(bars, C::B_O_FULL + i, oseg[i] & 1, abort_flag, tmo, role)) { ok = false; break; }
-          ++oseg[i];
-          tc_fence_after();
-          // total row sum: the two warpgroups' parts, added in a fixed order
-          lbuf[(i * 2 + g) * BM + row] = l_run[i];
-          mbar_arrive(bars + 8 * (C::B_LX + i));
-          if (!bwait_warp(bars, C::B_LX + i, lx[i] & 1, abort_flag, tmo, role)) { ok = false; break; }
-          ++lx[i];
-          const float l_tot = lbuf[(i * 2 + 0) * BM + row] + lbuf[(i * 2 + 1) * BM + row];
-          const uint32_t tO = tmem + lane_off + 256 + i * DP;
-          __half* obase = p.o + static_cast<long long>(bh) * p.Sq * p.D;
-          const int orow0 = q_row0 + i * BM + quad * 32;
-          if (t0 == 0 && t1 == p.n_tiles) {
-            // whole unit: O / l of this warpgroup's columns, 32 at a time
-            const float inv = 1.f / l_tot;
-#pragma unroll 1
-            for (int c = g * (DP / 64); c < (g + 1) * (DP / 64); ++c) {
-              uint32_t o[32];
-              tmem_ld32(tO + 32 * c, o);
-              tmem_wait_ld();
-              reg_fence32(o);
-              stage_32n(stg, lane, o, inv);
-              flush_stage_32n(stg, lane, obase, orow0, p.Sq, p.D, 32 * c);
-            }
-            continue;
-          }
-          // partial piece: unnormalised O columns of this warpgroup, (m, l)
-          // by warpgroup 0, into this CTA's workspace slot (chunk-major)
-          const int which = first_seg ? 0 : 1;
-          const long long slot = (static_cast<long long>(cta) * 2 + which) * 2 + i;
-          float* wo = p.ws_o + slot * BM * DP + row * 4;
-#pragma unroll 1
-          for (int c = g * (DP / 64); c < (g + 1) * (DP / 64); ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + 32 * c, o);
-            tmem_wait_ld();
-            reg_fence32(o);
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              *reinterpret_cast<float4*>(wo + (c * 8 + e) * BM * 4) =
-                  make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]), __uint_as_float(o[4 * e + 2]),
-                              __uint_as_float(o[4 * e + 3]));
-          }
-          if (g == 0) *reinterpret_cast<float2*>(p.ws_ml + (slot * BM + row) * 2) = make_float2(m_run[i], l_tot);
-          // Release: the tile rendezvous orders every thread's stores before
-          // thread 0's gpu-scope fence, which orders them before the counter.
-          if (!tile_sync(i)) { ok = false; break; }
-          const int rel = unit - p.tail_unit0;  // index of the unit within the split tail
-          unsigned long long* cnt = p.ws_cnt + rel * 2 + i;
-          const long long W = p.total_steps;
-          const int GT = p.tail_ctas;
-          const long long ubase = static_cast<long long>(rel) * p.n_tiles;
-          const int c_lo = owner_cta(ubase, W, GT);
-          const int c_hi = owner_cta(ubase + p.n_tiles - 1, W, GT);
-          if (warp == 0 && lane == 0) {
-            __threadfence();
-            // A counter whose tag is not this launch's epoch counts as 0.
-            unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(cnt), next;
-            while (true) {
-              next = (((cur >> 8) == p.epoch) ? cur : (p.epoch << 8)) + 1ull;
-              const unsigned long long seen = atomicCAS(cnt, cur, next);
-              if (seen == cur) break;
-              cur = seen;
-            }
-            const int last = (static_cast<int>(next & 0xffull) == c_hi - c_lo + 1) ? 1 : 0;
-            if (last) __threadfence();  // acquire: the other pieces' stores are visible
-            last_flag[i] = last;
-          }
-          if (!tile_sync(i)) { ok = false; break; }
-          if (!last_flag[i]) continue;
-          // Last piece to finish: combine every piece of this (unit, tile), in
-          // CTA order (deterministic bits), this warpgroup's columns.
-          const int np = c_hi - c_lo + 1;
-          auto piece_row = [&](int k) -> long long {
-            const int c2 = c_lo + k;
-            const int which2 = (static_cast<long long>(c2) * W >= ubase * GT) ? 0 : 1;
-            return ((static_cast<long long>(c2) * 2 + which2) * 2 + i) * BM + row;
-          };
-          auto piece_ml = [&](long long rb) -> float2 {
-            return __ldcg(reinterpret_cast<const float2*>(p.ws_ml + rb * 2));
-          };
-          float m_all = -INFINITY;
-#pragma unroll 1
-          for (int k = 0; k < np; ++k) m_all = fmaxf(m_all, piece_ml(piece_row(k)).x);
-          float l_all = 0.f;
-#pragma unroll 1
-          for (int k = 0; k < np; ++k) {
-            const float2 ml = piece_ml(piece_row(k));
-            l_all = fmaf(ml.y, ex2_approx(ml.x - m_all), l_all);
-          }
-          const float inv = 1.f / l_all;
-#pragma unroll 1
-          for (int c = g * (DP / 64); c < (g + 1) * (DP / 64); ++c) {
-            float acc[32];
-#pragma unroll
-            for (int e = 0; e < 32; ++e) acc[e] = 0.f;
-#pragma unroll 1
-            for (int k = 0; k < np; ++k) {
-              const long long rb = piece_row(k);
-              const float wk = ex2_approx(piece_ml(rb).x - m_all);
-              const long long sl = rb / BM;
-              const float* sbase = p.ws_o + sl * BM * DP + (rb - sl * BM) * 4;
-              float4 v4[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e)
-                v4[e] = __ldcg(reinterpret_cast<const float4*>(sbase + (c * 8 + e) * BM * 4));
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                acc[4 * e] = fmaf(v4[e].x, wk, acc[4 * e]);
-                acc[4 * e + 1] = fmaf(v4[e].y, wk, acc[4 * e + 1]);
-                acc[4 * e + 2] = fmaf(v4[e].z, wk, acc[4 * e + 2]);
-                acc[4 * e + 3] = fmaf(v4[e].w, wk, acc[4 * e + 3]);
-              }
-            }
-            uint32_t o[32];
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(acc[e]);
-            stage_32n(stg, lane, o, inv);
-            flush_stage_32n(stg, lane, obase, orow0, p.Sq, p.D, 32 * c);
-          }
-        }
-      }
-    } else {
     const int ti = warp >> 2;  // query tile
     const int quad = warp & 3; // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
@@ -1295,7 +959,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         q_row0 + ti * BM + quad * 32, p.Sq, p.D, 64 * (c >> 1));
         }
       }
-    }
     }
   }
 
