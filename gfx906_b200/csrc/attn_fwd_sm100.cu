@@ -470,6 +470,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const unsigned long long tmo = p.timeout_ns;
+  // Everything above touches no global memory; from here on the previous
+  // kernel on the stream (which may have written q, k, v, o or the
+  // workspace) must be complete. The next kernel may then be launched: its
+  // CTAs take SMs only as this grid's CTAs exit.
+  griddep_wait();
+  if (threadIdx.x == 0) griddep_launch_dependents();
 
   if (warp >= 8) setmaxnreg_dec<REGS_CONTROL>();  // whole control warpgroup, one instruction
   if (warp == PRODUCER_WARP) {
@@ -932,22 +938,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           float acc[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+          // pieces two at a time: the loads of both are in flight together
+          // (L2 latency, not bandwidth, bounds this loop); the accumulation
+          // order is still piece 0, 1, 2, ...
 #pragma unroll 1
-          for (int k = 0; k < np; ++k) {
-            const long long rb = piece_row(k);
-            const float wk = ex2_approx(piece_ml(rb).x - m_all);
-            // chunk-major slot (see the partial write): chunk q of this row
-            const long long sl = rb / BM;
-            const float* sbase = p.ws_o + sl * BM * DP + (rb - sl * BM) * 4;
-            float4 v4[8];
+          for (int k0 = 0; k0 < np; k0 += 2) {
+            float4 v4[2][8];
+            float wk[2];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v4[e] = __ldcg(reinterpret_cast<const float4*>(sbase + (c * 8 + e) * BM * 4));
+            for (int kk = 0; kk < 2; ++kk) {
+              const int k = (k0 + kk < np) ? k0 + kk : k0;  // a duplicate load, never accumulated
+              const long long rb = piece_row(k);
+              wk[kk] = ex2_approx(piece_ml(rb).x - m_all);
+              // chunk-major slot (see the partial write): chunk q of this row
+              const long long sl = rb / BM;
+              const float* sbase = p.ws_o + sl * BM * DP + (rb - sl * BM) * 4;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              acc[4 * e] = fmaf(v4[e].x, wk, acc[4 * e]);
-              acc[4 * e + 1] = fmaf(v4[e].y, wk, acc[4 * e + 1]);
-              acc[4 * e + 2] = fmaf(v4[e].z, wk, acc[4 * e + 2]);
-              acc[4 * e + 3] = fmaf(v4[e].w, wk, acc[4 * e + 3]);
+              for (int e = 0; e < 8; ++e)
+                v4[kk][e] = __ldcg(reinterpret_cast<const float4*>(sbase + (c * 8 + e) * BM * 4));
+            }
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+              if (k0 + kk < np) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  acc[4 * e] = fmaf(v4[kk][e].x, wk[kk], acc[4 * e]);
+                  acc[4 * e + 1] = fmaf(v4[kk][e].y, wk[kk], acc[4 * e + 1]);
+                  acc[4 * e + 2] = fmaf(v4[kk][e].z, wk[kk], acc[4 * e + 2]);
+                  acc[4 * e + 3] = fmaf(v4[kk][e].w, wk[kk], acc[4 * e + 3]);
+                }
+              }
             }
           }
           uint32_t o[32];
@@ -1055,6 +1075,8 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();  // the previous kernel on the stream is complete (see attn_fwd_kernel)
+  if (threadIdx.x == 0) griddep_launch_dependents();
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
@@ -1527,6 +1549,34 @@ size_t workspace_bytes(const Plan& pl, int DP) {
          align256(slots * 2 * sizeof(float)) + slots * DP * sizeof(float);
 }
 
+// Launches a kernel with programmatic stream serialization: back-to-back
+// calls on one stream then overlap the next call's launch and set-up with the
+// end of this one (measured on B200: 5-6 us from the last CTA's exit to the
+// next launch's first CTA without it). The kernels wait for the previous
+// grid before their first global-memory access, so results and ordering are
+// those of a plain launch. Falls back to a plain launch if the attribute is
+// refused.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    cfg.numAttrs = 0;
+    e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  }
+  return (e == cudaSuccess && cudaGetLastError() == cudaSuccess) ? GFX906_B200_OK : GFX906_B200_ECUDA;
+}
+
 template <int DP>
 int launch_dp(const void* q, const void* k, const void* v, void* o, long long BH, int Sq, int Skv, int D,
               float scale, void* ws, size_t ws_size, int dev, cudaStream_t stream) {
@@ -1564,8 +1614,8 @@ int launch_dp(const void* q, const void* k, const void* v, void* o, long long BH
     base += align256(slots * 2 * sizeof(float));
     prm.ws_o = reinterpret_cast<float*>(base);
   }
-  fa::attn_fwd_kernel<DP><<<pl.G, fa::NUM_THREADS, fa::Cfg<DP>::SMEM_BYTES, stream>>>(mq, mk, mv, prm);
-  return cudaGetLastError() == cudaSuccess ? GFX906_B200_OK : GFX906_B200_ECUDA;
+  return launch_pdl(fa::attn_fwd_kernel<DP>, dim3(pl.G), dim3(fa::NUM_THREADS), fa::Cfg<DP>::SMEM_BYTES, stream,
+                    mq, mk, mv, prm);
 }
 
 template <bool DMAJOR>
@@ -1591,8 +1641,9 @@ int launch_d512(const void* q, const void* k, const void* v, void* o, long long 
     const long long n = (BH - off) < 65535 ? (BH - off) : 65535;
     prm.bh_offset = static_cast<int>(off);
     dim3 grid(2 * qtiles, static_cast<unsigned>(n), 1);
-    fa::attn_fwd_d512_kernel<DMAJOR><<<grid, fa::Cfg512::THREADS, fa::Cfg512::SMEM_BYTES, stream>>>(mq, mk, mv, mo, prm);
-    if (cudaGetLastError() != cudaSuccess) return GFX906_B200_ECUDA;
+    const int rc = launch_pdl(fa::attn_fwd_d512_kernel<DMAJOR>, grid, dim3(fa::Cfg512::THREADS),
+                              fa::Cfg512::SMEM_BYTES, stream, mq, mk, mv, mo, prm);
+    if (rc != GFX906_B200_OK) return rc;
   }
   return GFX906_B200_OK;
 }

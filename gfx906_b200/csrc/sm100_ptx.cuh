@@ -55,6 +55,17 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthread
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// ------------------------------------------------- programmatic dependent launch
+// Blocks until the grids this grid depends on (the previous kernel on the
+// stream, when this one was launched with programmatic stream serialization)
+// have completed and their memory is visible; returns at once otherwise.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next grid on the stream be launched before this one completes (its
+// CTAs then run their set-up as SMs free up and wait in griddep_wait).
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // --------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
