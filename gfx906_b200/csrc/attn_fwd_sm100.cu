@@ -1325,6 +1325,360 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
   }
 }
 
+// ------------------------------------------------- D = 512 on CTA pairs
+// The same head-dim-half split as attn_fwd_d512_kernel, with two query tiles
+// of one (batch, head) and one head-dim half per 2-CTA cluster. The even CTA
+// (the leader) issues every MMA with cta_group::2: M = 256 rows, 128 from each
+// CTA's Q tile, D in each CTA's own TMEM. Each CTA loads only half of the B
+// operands into its shared memory: keys 64 r .. 64 r + 63 of every K tile and
+// head dims 128 r .. 128 r + 127 of its half of every V tile (r = CTA rank),
+// so a CTA streams 96 KiB per key tile instead of 192 KiB and its three 32 KiB
+// ring slots each feed 1024 tensor cycles instead of 512. Measured on the
+// single-CTA kernel: the MMA warp waited 19% of its loop for K/V data.
+//
+// Ring slots per key tile j (both CTAs, the same sequence): K(j) head dims
+// 0-255, K(j) head dims 256-511, then V(j-1). A slot of K is four 8 KiB
+// [64 keys x 64 dims] boxes; a slot of V two 16 KiB [128 keys x 64 dims] boxes.
+//
+// Protocol (per slot phase): each producer waits for its own KV_EMPTY (the
+// leader's MMA commit arrives in both CTAs), the leader's producer arms the
+// leader's KV_FULL for the bytes of both CTAs, and both CTAs' loads complete on
+// the leader's KV_FULL. The leader's MMA warp waits on KV_FULL and on P_FULL,
+// which both softmax warpgroups arrive at (the odd CTA's remotely); S_FULL,
+// PV_DONE and O_FULL are multicast commits that arrive in both CTAs.
+struct Cfg512P {
+  static constexpr int SLOTS = 3;
+  static constexpr int SLOT_BYTES = 2 * CHUNK_BYTES;
+  static constexpr int Q_BYTES = 8 * CHUNK_BYTES;
+  static constexpr int DATA_BYTES = Q_BYTES + SLOTS * SLOT_BYTES;
+  static constexpr int B_Q = 0, B_KV_FULL = 1, B_KV_EMPTY = 1 + SLOTS, B_S_FULL = 1 + 2 * SLOTS;
+  static constexpr int B_P_FULL = B_S_FULL + 2, B_PV_DONE = B_P_FULL + 2, B_O_FULL = B_PV_DONE + 1;
+  static constexpr int B_DRAIN = B_O_FULL + 1, B_EPI = B_DRAIN + 1, NUM_BARS = B_EPI + 1;
+  static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int THREADS = 256;
+  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+};
+
+__device__ __forceinline__ bool bwait_cluster_warp(uint32_t bars, int idx, uint32_t parity, volatile int* abort_flag,
+                                                   unsigned long long timeout_ns, int role) {
+  const uint32_t bar = bars + 8u * idx;
+  bool ok = mbar_try_wait_cluster(bar, parity);
+  if (!ok) {
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t n = 0;
+    while (true) {
+      if (mbar_try_wait_cluster(bar, parity)) { ok = true; break; }
+      if (*abort_flag) break;
+      if ((++n & 31u) == 0u) {
+        const uint64_t t = globaltimer_ns();
+        if (t - t0 > timeout_ns || n > (1u << 24)) {
+          *abort_flag = 1;
+          if (atomicCAS(&g_status, 0u, 1u) == 0u) {
+            g_timeout_info[0] = blockIdx.x;
+            g_timeout_info[1] = blockIdx.y;
+            g_timeout_info[2] = threadIdx.x / 32;
+            g_timeout_info[3] = idx;
+            g_timeout_info[4] = static_cast<int>(parity);
+            g_timeout_info[5] = role;
+            __threadfence();
+          } else {
+            atomicOr(&g_status, 1u);
+          }
+          break;
+        }
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
+__global__ void __launch_bounds__(Cfg512P::THREADS, 1)
+    attn_fwd_d512_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                              const Params p) {
+  using C = Cfg512P;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t s0 = (raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (s0 - raw);
+  const uint32_t sQ = s0;
+  const uint32_t sRing = s0 + C::Q_BYTES;
+  const uint32_t bars = s0 + C::DATA_BYTES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::DATA_BYTES + C::NUM_BARS * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* drain_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();  // 0: leader (issues the MMAs), 1: peer
+  const bool leader = rank == 0;
+  const int bh = blockIdx.y + p.bh_offset;
+  const int pair = blockIdx.x >> 1;  // (query tile pair, head-dim half)
+  const int half = pair & 1;
+  const int q_row0 = ((pair >> 1) * 2 + static_cast<int>(rank)) * BM;
+  const int n_tiles = (p.Skv + BN - 1) / BN;
+  const unsigned long long tmo = p.timeout_ns;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bars + 8 * C::B_Q, 1);
+    for (int s = 0; s < C::SLOTS; ++s) {
+      mbar_init(bars + 8 * (C::B_KV_FULL + s), 1);
+      mbar_init(bars + 8 * (C::B_KV_EMPTY + s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bars + 8 * (C::B_S_FULL + i), 1);
+      mbar_init(bars + 8 * (C::B_P_FULL + i), 2 * BM);  // both CTAs' softmax threads (leader's barrier)
+    }
+    mbar_init(bars + 8 * C::B_PV_DONE, 1);
+    mbar_init(bars + 8 * C::B_O_FULL, 1);
+    mbar_init(bars + 8 * C::B_DRAIN, 1);
+    mbar_init(bars + 8 * C::B_EPI, BM);
+    *abort_flag = 0;
+    *drain_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 5) {
+    tmem_alloc2(smem_u32(tmem_slot), 512);
+    tmem_relinquish2();
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any cross-CTA arrival
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+  if (threadIdx.x == 0) griddep_launch_dependents();
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_o);
+    const uint32_t lead_q = mapa_shared(bars + 8 * C::B_Q, 0);
+    if (leader) mbar_arrive_expect_tx_warp(bars + 8 * C::B_Q, 2 * C::Q_BYTES);
+    for (int c = 0; c < 8; ++c) tma_load_3d_pair_warp(sQ + c * CHUNK_BYTES, &tm_q, lead_q, c * 64, q_row0, bh);
+    int it = 0;
+    bool ok = true;
+    auto slot_begin = [&](int& slot, uint32_t& lead_full) -> bool {
+      slot = it % C::SLOTS;
+      const uint32_t ph = (it / C::SLOTS) & 1;
+      if (!bwait_warp(bars, C::B_KV_EMPTY + slot, ph ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) return false;
+      if (leader) mbar_arrive_expect_tx_warp(bars + 8 * (C::B_KV_FULL + slot), 2 * C::SLOT_BYTES);
+      lead_full = mapa_shared(bars + 8 * (C::B_KV_FULL + slot), 0);
+      ++it;
+      return true;
+    };
+    for (int j = 0; j <= n_tiles && ok; ++j) {
+      if (j < n_tiles) {
+        // K(j): keys j*128 + 64*rank .. +63, head dims 256 s .. 256 s + 255
+        for (int s = 0; s < 2 && ok; ++s) {
+          int slot;
+          uint32_t lf;
+          if (!(ok = slot_begin(slot, lf))) break;
+#pragma unroll
+          for (int b = 0; b < 4; ++b)
+            tma_load_3d_pair_warp(sRing + slot * C::SLOT_BYTES + b * 8192, &tm_k, lf, 256 * s + 64 * b,
+                                  j * BN + 64 * static_cast<int>(rank), bh);
+        }
+      }
+      if (j > 0 && ok) {
+        // V(j-1): keys (j-1)*128 .. +127, head dims 256 half + 128 rank .. +127
+        int slot;
+        uint32_t lf;
+        if (!(ok = slot_begin(slot, lf))) break;
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
+          tma_load_3d_pair_warp(sRing + slot * C::SLOT_BYTES + b * CHUNK_BYTES, &tm_v, lf,
+                                256 * half + 128 * static_cast<int>(rank) + 64 * b, (j - 1) * BN, bh);
+      }
+    }
+    if (!ok && leader) {
+      // Drain: every load issued must land before shared memory goes away.
+      if (!mbar_try_wait(bars + 8 * C::B_Q, 0))
+        wait_slow(bars + 8 * C::B_Q, 0, drain_flag, 100000000ull, C::B_Q, ROLE_PRODUCER);
+      const int first = it > C::SLOTS ? it - C::SLOTS : 0;
+      for (int t = first; t < it; ++t) {
+        const int slot = t % C::SLOTS;
+        const uint32_t ph = (t / C::SLOTS) & 1;
+        if (!mbar_try_wait(bars + 8 * (C::B_KV_FULL + slot), ph))
+          wait_slow(bars + 8 * (C::B_KV_FULL + slot), ph, drain_flag, 100000000ull, C::B_KV_FULL + slot,
+                    ROLE_PRODUCER);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5 && leader) {
+    // ----------------------------------------------------------- MMA issuer
+    constexpr uint32_t IDESC_QK = idesc_f16_f32(2 * BM, BN, 0, 0);   // M = 256 over the pair, N = 128 keys
+    constexpr uint32_t IDESC_PV = idesc_f16_f32(2 * BM, 256, 0, 1);  // N = 256 head dims of this half
+    const uint64_t dQ = sdesc_sw128(sQ, 16, 1024);
+    const uint64_t dK = sdesc_sw128(sRing, 16, 1024);             // K-major [64 keys x 64 dims] boxes
+    const uint64_t dV = sdesc_sw128(sRing, CHUNK_BYTES, 1024);    // MN-major, 64-dim blocks 16 KiB apart
+    const uint32_t tO = tmem + 256;
+    constexpr uint16_t BOTH = 0x3;
+    int it = 0;
+    bool ok = bwait_warp(bars, C::B_Q, 0, abort_flag, tmo, ROLE_MMA);
+    tc_fence_after();
+    auto next_slot = [&](int& slot) -> bool {
+      slot = it % C::SLOTS;
+      const uint32_t ph = (it / C::SLOTS) & 1;
+      ++it;
+      if (!bwait_warp(bars, C::B_KV_FULL + slot, ph, abort_flag, tmo, ROLE_MMA)) return false;
+      tc_fence_after();
+      return true;
+    };
+    auto issue_s = [&](int j) -> bool {
+      const uint32_t tS = tmem + 128 * (j & 1);
+      for (int s = 0; s < 2; ++s) {
+        int slot;
+        if (!next_slot(slot)) return false;
+        const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          // head dims 256 s + 64 b ..: Q chunk 4 s + b, K box b; 16 dims = 32 bytes
+          const uint64_t qa = dQ + (static_cast<uint32_t>((4 * s + b) * CHUNK_BYTES) >> 4);
+          const uint64_t kb = dK + soff + (static_cast<uint32_t>(b * 8192) >> 4);
+          mma4_ss_pair_warp(tS, qa, qa + 2, qa + 4, qa + 6, kb, kb + 2, kb + 4, kb + 6, IDESC_QK,
+                            (s > 0 || b > 0) ? 1u : 0u);
+        }
+        tc_commit_pair_mc_warp(bars + 8 * (C::B_KV_EMPTY + slot), BOTH);
+      }
+      tc_commit_pair_mc_warp(bars + 8 * (C::B_S_FULL + (j & 1)), BOTH);
+      return true;
+    };
+    auto issue_pv = [&](int j) -> bool {
+      if (!bwait_cluster_warp(bars, C::B_P_FULL + (j & 1), (j >> 1) & 1, abort_flag, tmo, ROLE_MMA)) return false;
+      tc_fence_after();
+      const uint32_t tP = tmem + 128 * (j & 1);
+      int slot;
+      if (!next_slot(slot)) return false;
+      const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        // keys 64 c .. 64 c + 63: P columns 32 c .., V rows 2048 bytes per 16 keys
+        const uint64_t vb = dV + soff + (static_cast<uint32_t>(4 * c * 2048) >> 4);
+        mma4_ts_pair_warp(tO, tP + 32 * c, vb, vb + 128, vb + 256, vb + 384, IDESC_PV, (j > 0 || c > 0) ? 1u : 0u);
+      }
+      tc_commit_pair_mc_warp(bars + 8 * (C::B_KV_EMPTY + slot), BOTH);
+      tc_commit_pair_mc_warp(bars + 8 * C::B_PV_DONE, BOTH);
+      return true;
+    };
+    for (int j = 0; j <= n_tiles && ok; ++j) {
+      if (j < n_tiles) ok = issue_s(j);
+      if (ok && j > 0) ok = issue_pv(j - 1);
+    }
+    if (ok) {
+      tc_commit_pair_mc_warp(bars + 8 * C::B_O_FULL, BOTH);
+    } else {
+      tc_commit_pair_mc_warp(bars + 8 * C::B_DRAIN, 0x1);
+      wait_slow(bars + 8 * C::B_DRAIN, 0, drain_flag, 100000000ull, C::B_DRAIN, ROLE_MMA);
+    }
+    __syncwarp();
+  } else if (warp < 4) {
+    // ------------------------------------------------------------- softmax
+    const int row = warp * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tO = tmem + lane_off + 256;
+    const float sl2 = p.scale_log2;
+    const bool pos = sl2 >= 0.f;
+    const uint32_t p_full0 = mapa_shared(bars + 8 * C::B_P_FULL, 0);  // the leader's P_FULL[0]
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int b = j & 1;
+      const uint32_t tS = tmem + lane_off + 128 * b;
+      if (!bwait_warp(bars, C::B_S_FULL + b, (j >> 1) & 1, abort_flag, tmo, ROLE_SOFTMAX0)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + 32 * c, s + 32 * c);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) reg_fence32(s + 32 * c);
+      const int nvalid = min(BN, p.Skv - j * BN);
+      const bool full = nvalid == BN;
+      const float mx = row_extreme(s, nvalid, full, pos);
+      const float m_new = fmaxf(m_run, mx * sl2);
+      const bool need = m_new > m_run + RESCALE_THRESHOLD;
+      float factor = 1.f;
+      if (need) {
+        factor = ex2_approx(m_run - m_new);
+        m_run = m_new;
+      }
+      l_run *= factor;
+      float lsum0, lsum1;
+      if (full)
+        row_exp_store<false>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {}, [] {});
+      else
+        row_exp_store<true>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {}, [] {});
+      l_run += lsum0 + lsum1;
+      // O may only be rescaled once PV(j-1) has completed.
+      if (j > 0) {
+        if (!bwait_warp(bars, C::B_PV_DONE, (j - 1) & 1, abort_flag, tmo, ROLE_SOFTMAX0)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+          for (int c = 0; c < 256 / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + 32 * c, o);
+            tmem_wait_ld();
+            reg_fence32(o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+            tmem_st32(tO + 32 * c, o);
+          }
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive_remote(p_full0 + 8u * b);  // the leader's P_FULL[b] (this CTA's, on the leader)
+    }
+    const bool have_o = ok && n_tiles > 0 && bwait_warp(bars, C::B_O_FULL, 0, abort_flag, tmo, ROLE_SOFTMAX0);
+    if (have_o) {
+      tc_fence_after();
+      const float inv = 1.f / l_run;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[64];
+        tmem_ld32(tO + 64 * c, o);
+        tmem_ld32(tO + 64 * c + 32, o + 32);
+        tmem_wait_ld();
+        reg_fence32(o);
+        reg_fence32(o + 32);
+        // Q is dead (its last MMA completed): it becomes the staging buffer
+        const uint32_t rowbase = sQ + c * CHUNK_BYTES + row * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint32_t a = pack_half2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
+          const uint32_t bb = pack_half2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
+          const uint32_t cc = pack_half2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
+          const uint32_t d = pack_half2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
+          st_shared_v4(rowbase + ((u ^ (row & 7)) << 4), a, bb, cc, d);
+        }
+      }
+      fence_proxy_async_smem();
+    }
+    mbar_arrive(bars + 8 * C::B_EPI);
+    // (the odd CTA of the last pair may hold rows past Sq only: nothing to store)
+    if (warp == 0 && lane == 0 && have_o && q_row0 < p.Sq && bwait(bars, C::B_EPI, 0, abort_flag, tmo, ROLE_SOFTMAX0)) {
+      for (int c = 0; c < 4; ++c) tma_store_3d(&tm_o, sQ + c * CHUNK_BYTES, 256 * half + 64 * c, q_row0, bh);
+      tma_store_commit();
+      tma_store_wait_read0();
+    }
+  }
+
+  // Neither CTA may release its shared memory or TMEM while the other (or
+  // the leader's MMAs) may still use them.
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc2(tmem, 512);
+  }
+}
+
 // Self-test kernel: one thread waits on an mbarrier nothing arrives at.
 __global__ void wait_timeout_selftest_kernel(unsigned long long timeout_ns) {
   __shared__ __align__(8) uint64_t bar;
@@ -1435,7 +1789,9 @@ int check_device(int* dev_out) {
         cudaFuncSetAttribute(fa::attn_fwd_d512_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              fa::Cfg512::SMEM_BYTES) != cudaSuccess ||
         cudaFuncSetAttribute(fa::attn_fwd_d512_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             fa::Cfg512::SMEM_BYTES) != cudaSuccess)
+                             fa::Cfg512::SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(fa::attn_fwd_d512_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             fa::Cfg512P::SMEM_BYTES) != cudaSuccess)
       return GFX906_B200_ECUDA;
     di.attrs_set = true;
   }
@@ -1556,22 +1912,28 @@ size_t workspace_bytes(const Plan& pl, int DP) {
 // grid before their first global-memory access, so results and ordering are
 // those of a plain launch. Falls back to a plain launch if the attribute is
 // refused.
+// cluster_x > 1 launches clusters of that many CTAs along x.
 template <typename... KArgs, typename... Args>
-int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t stream, Args... args) {
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t stream, int cluster_x,
+               Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster_x);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
   if (e != cudaSuccess) {
     (void)cudaGetLastError();
-    cfg.numAttrs = 0;
+    cfg.numAttrs = 1;  // without programmatic serialization
     e = cudaLaunchKernelEx(&cfg, kernel, args...);
   }
   return (e == cudaSuccess && cudaGetLastError() == cudaSuccess) ? GFX906_B200_OK : GFX906_B200_ECUDA;
@@ -1614,7 +1976,7 @@ int launch_dp(const void* q, const void* k, const void* v, void* o, long long BH
     base += align256(slots * 2 * sizeof(float));
     prm.ws_o = reinterpret_cast<float*>(base);
   }
-  return launch_pdl(fa::attn_fwd_kernel<DP>, dim3(pl.G), dim3(fa::NUM_THREADS), fa::Cfg<DP>::SMEM_BYTES, stream,
+  return launch_pdl(fa::attn_fwd_kernel<DP>, dim3(pl.G), dim3(fa::NUM_THREADS), fa::Cfg<DP>::SMEM_BYTES, stream, 1,
                     mq, mk, mv, prm);
 }
 
@@ -1642,7 +2004,34 @@ int launch_d512(const void* q, const void* k, const void* v, void* o, long long 
     prm.bh_offset = static_cast<int>(off);
     dim3 grid(2 * qtiles, static_cast<unsigned>(n), 1);
     const int rc = launch_pdl(fa::attn_fwd_d512_kernel<DMAJOR>, grid, dim3(fa::Cfg512::THREADS),
-                              fa::Cfg512::SMEM_BYTES, stream, mq, mk, mv, mo, prm);
+                              fa::Cfg512::SMEM_BYTES, stream, 1, mq, mk, mv, mo, prm);
+    if (rc != GFX906_B200_OK) return rc;
+  }
+  return GFX906_B200_OK;
+}
+
+// D = 512 (row-major) on CTA pairs: grid x = 2 CTAs x 2 head-dim halves x
+// ceil(query tiles / 2) pairs, clusters of 2 along x.
+int launch_d512_pair(const void* q, const void* k, const void* v, void* o, long long BH, int Sq, int Skv, float scale,
+                     cudaStream_t stream) {
+  CUtensorMap mq, mk, mv, mo;
+  if (!make_map(&mq, q, 512, Sq, BH, fa::BM) || !make_map(&mk, k, 512, Skv, BH, fa::BN / 2) ||
+      !make_map(&mv, v, 512, Skv, BH, fa::BN) || !make_map(&mo, o, 512, Sq, BH, fa::BM))
+    return GFX906_B200_ECUDA;
+  fa::Params prm{};
+  prm.Sq = Sq;
+  prm.Skv = Skv;
+  prm.D = 512;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.timeout_ns = timeout_ns_from_env();
+  const long long qtiles = (Sq + fa::BM - 1) / fa::BM;
+  const long long gx = 4 * ((qtiles + 1) / 2);
+  if (gx > 0x7fffffffll) return GFX906_B200_EINVAL;
+  for (long long off = 0; off < BH; off += 65535) {
+    const long long n = (BH - off) < 65535 ? (BH - off) : 65535;
+    prm.bh_offset = static_cast<int>(off);
+    const int rc = launch_pdl(fa::attn_fwd_d512_pair_kernel, dim3(static_cast<unsigned>(gx), static_cast<unsigned>(n), 1),
+                              dim3(fa::Cfg512P::THREADS), fa::Cfg512P::SMEM_BYTES, stream, 2, mq, mk, mv, mo, prm);
     if (rc != GFX906_B200_OK) return rc;
   }
   return GFX906_B200_OK;
@@ -1688,7 +2077,7 @@ int attn_launch_impl(const void* q, const void* k, const void* v, void* o, int B
   }
   if (D == 128) return launch_dp<128>(q, k, v, o, BH, Sq, Skv, D, scale, ws, ws_size, dev, stream);
   if (D <= 64) return launch_dp<64>(q, k, v, o, BH, Sq, Skv, D, scale, ws, ws_size, dev, stream);
-  return launch_d512<false>(q, k, v, o, BH, Sq, Skv, scale, stream);
+  return launch_d512_pair(q, k, v, o, BH, Sq, Skv, scale, stream);
 }
 
 }  // namespace
@@ -1759,7 +2148,7 @@ int gfx906_b200_attn_plan(int B, int H, int Sq, int Skv, int D, int with_workspa
   }
   const long long BH = static_cast<long long>(B) * H;
   if (D == 512) {
-    const long long ctas = 2ll * ((Sq + fa::BM - 1) / fa::BM) * BH;
+    const long long ctas = 4ll * (((Sq + fa::BM - 1) / fa::BM + 1) / 2) * BH;
     out4[0] = static_cast<int>(ctas < 0x7fffffffll ? ctas : 0x7fffffffll);
     out4[3] = fa::BM;
     return GFX906_B200_OK;

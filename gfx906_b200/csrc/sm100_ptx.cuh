@@ -235,6 +235,108 @@ __device__ __forceinline__ void tc_commit_warp(uint32_t bar) {
       : "memory");
 }
 
+// ------------------------------------------------ CTA pairs (cta_group::2)
+// Two CTAs of a cluster run one MMA stream together: an instruction issued by
+// the even CTA (the leader) computes M = 256 rows, 128 in each CTA's TMEM; the
+// A operand rows and one half of the B operand's N columns come from each
+// CTA's shared memory at the same offsets.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Arrive on an mbarrier of another CTA of the cluster (cluster-scope release).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// try_wait with cluster-scope acquire: pairs with arrivals made by the other CTA.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// All threads of both CTAs: every thread of the cluster arrives, then waits.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc2(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// 3-D tiled load into this CTA's shared memory whose completion is counted on
+// an mbarrier of either CTA of the pair (`bar` is a shared::cluster address).
+// No multicast: each CTA loads only into its own shared memory.
+__device__ __forceinline__ void tma_load_3d_pair_warp(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0,
+                                                      int c1, int c2) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];\n\t}" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+// Four pair MMAs accumulating into one D (see mma4_ss_warp), SS and TS forms.
+__device__ __forceinline__ void mma4_ss_pair_warp(uint32_t d, uint64_t a0, uint64_t a1, uint64_t a2, uint64_t a3,
+                                                  uint64_t b0, uint64_t b1, uint64_t b2, uint64_t b3, uint32_t idesc,
+                                                  uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred e, p, t;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %10, 0;\n\t"
+      "setp.eq.b32 t, 0, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %5, %9, p;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %2, %6, %9, t;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %3, %7, %9, t;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %4, %8, %9, t;\n\t}" ::"r"(d),
+      "l"(a0), "l"(a1), "l"(a2), "l"(a3), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(idesc), "r"(acc0)
+      : "memory");
+}
+__device__ __forceinline__ void mma4_ts_pair_warp(uint32_t d, uint32_t a, uint64_t b0, uint64_t b1, uint64_t b2,
+                                                  uint64_t b3, uint32_t idesc, uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred e, p, t;\n\t.reg .b32 a1, a2, a3;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %7, 0;\n\t"
+      "setp.eq.b32 t, 0, 0;\n\t"
+      "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %6, p;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [a1], %3, %6, t;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [a2], %4, %6, t;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [a3], %5, %6, t;\n\t}" ::"r"(d),
+      "r"(a), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(idesc), "r"(acc0)
+      : "memory");
+}
+// Arrive once on the mbarrier at `bar` (a local shared::cta offset) in every
+// CTA of cta_mask when all pair MMAs this thread issued have completed.
+__device__ __forceinline__ void tc_commit_pair_mc_warp(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+
 // Instruction descriptor, kind::f16: fp16 A and B, fp32 D, dense.
 //   [4,6) D format (1 = f32); [7,10) A format (0 = f16); [10,13) B format;
 //   [15] A major (0 = K, 1 = MN); [16] B major; [17,23) N>>3; [24,29) M>>4.
