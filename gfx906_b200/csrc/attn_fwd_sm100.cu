@@ -1326,15 +1326,23 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
 }
 
 // ------------------------------------------------- D = 512 on CTA pairs
-// The same head-dim-half split as attn_fwd_d512_kernel, with two query tiles
-// of one (batch, head) and one head-dim half per 2-CTA cluster. The even CTA
-// (the leader) issues every MMA with cta_group::2: M = 256 rows, 128 from each
-// CTA's Q tile, D in each CTA's own TMEM. Each CTA loads only half of the B
-// operands into its shared memory: keys 64 r .. 64 r + 63 of every K tile and
-// head dims 128 r .. 128 r + 127 of its half of every V tile (r = CTA rank),
-// so a CTA streams 96 KiB per key tile instead of 192 KiB and its three 32 KiB
-// ring slots each feed 1024 tensor cycles instead of 512. Measured on the
-// single-CTA kernel: the MMA warp waited 19% of its loop for K/V data.
+// The head-dim-half split of attn_fwd_d512_kernel, run on 2-CTA clusters: a
+// work unit is two query tiles of one (batch, head) and one head-dim half,
+// one query tile per CTA. The even CTA (the leader) issues every MMA with
+// cta_group::2: M = 256 rows, 128 from each CTA's Q tile, D in each CTA's own
+// TMEM. Each CTA loads only half of the B operands into its shared memory:
+// keys 64 r .. 64 r + 63 of every K tile and head dims 128 r .. 128 r + 127
+// of its half of every V tile (r = CTA rank), so a CTA streams 96 KiB per key
+// tile instead of 192 KiB and its three 32 KiB ring slots each feed 1024
+// tensor cycles instead of 512 (measured on the single-CTA kernel: its MMA
+// warp waited 19% of the time for K/V data; here 11%).
+//
+// Persistent: one cluster per SM pair walks a list of segments (unit, first
+// key tile, end key tile) with the schedule of attn_fwd_kernel (SegIter over
+// clusters): whole units first, then, in split mode, the key range of the
+// last partial wave cut into contiguous step ranges per cluster, partial
+// results combined by the last piece to finish (one combine per unit and
+// CTA rank). Without it 256 one-shot CTAs (C4) made 1.73 waves on 148 SMs.
 //
 // Ring slots per key tile j (both CTAs, the same sequence): K(j) head dims
 // 0-255, K(j) head dims 256-511, then V(j-1). A slot of K is four 8 KiB
@@ -1343,19 +1351,23 @@ __global__ void __launch_bounds__(Cfg512::THREADS, 1)
 // Protocol (per slot phase): each producer waits for its own KV_EMPTY (the
 // leader's MMA commit arrives in both CTAs), the leader's producer arms the
 // leader's KV_FULL for the bytes of both CTAs, and both CTAs' loads complete on
-// the leader's KV_FULL. The leader's MMA warp waits on KV_FULL and on P_FULL,
-// which both softmax warpgroups arrive at (the odd CTA's remotely); S_FULL,
-// PV_DONE and O_FULL are multicast commits that arrive in both CTAs.
+// the leader's KV_FULL; Q the same way per segment, after this CTA's Q_EMPTY
+// (its previous segment's epilogue has released the Q buffer, which stages a
+// whole unit's output for its TMA store). The leader's MMA warp waits on
+// KV_FULL and on P_FULL, which both softmax warpgroups arrive at (the odd
+// CTA's remotely); S_FULL, PV_DONE and O_FULL are multicast commits that
+// arrive in both CTAs.
 struct Cfg512P {
   static constexpr int SLOTS = 3;
   static constexpr int SLOT_BYTES = 2 * CHUNK_BYTES;
   static constexpr int Q_BYTES = 8 * CHUNK_BYTES;
   static constexpr int DATA_BYTES = Q_BYTES + SLOTS * SLOT_BYTES;
-  static constexpr int B_Q = 0, B_KV_FULL = 1, B_KV_EMPTY = 1 + SLOTS, B_S_FULL = 1 + 2 * SLOTS;
+  static constexpr int B_Q = 0, B_Q_EMPTY = 1, B_KV_FULL = 2, B_KV_EMPTY = 2 + SLOTS, B_S_FULL = 2 + 2 * SLOTS;
   static constexpr int B_P_FULL = B_S_FULL + 2, B_PV_DONE = B_P_FULL + 2, B_O_FULL = B_PV_DONE + 1;
-  static constexpr int B_DRAIN = B_O_FULL + 1, B_EPI = B_DRAIN + 1, NUM_BARS = B_EPI + 1;
+  static constexpr int B_DRAIN = B_O_FULL + 1, B_EPI = B_DRAIN + 1, B_WG = B_EPI + 1, NUM_BARS = B_WG + 1;
   static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 256;
+  static constexpr int DH = 256;  // head dims per CTA pair (one half of D = 512)
   static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
 
@@ -1392,6 +1404,18 @@ __device__ __forceinline__ bool bwait_cluster_warp(uint32_t bars, int idx, uint3
   return __all_sync(0xffffffffu, ok);
 }
 
+// Unit u of the D = 512 pair schedule: p.n_qb units per (batch, head), each
+// (query tile pair, head-dim half); this CTA's query rows and head-dim half.
+struct Unit512 {
+  int bh, half, q_row0;
+  __device__ __forceinline__ Unit512(const Params& p, int u, uint32_t rank) {
+    bh = u / p.n_qb;
+    const int rem = u - bh * p.n_qb;
+    half = rem & 1;
+    q_row0 = ((rem >> 1) * 2 + static_cast<int>(rank)) * BM;
+  }
+};
+
 __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
     attn_fwd_d512_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -1407,20 +1431,19 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::DATA_BYTES + C::NUM_BARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* drain_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 3);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();  // 0: leader (issues the MMAs), 1: peer
   const bool leader = rank == 0;
-  const int bh = blockIdx.y + p.bh_offset;
-  const int pair = blockIdx.x >> 1;  // (query tile pair, head-dim half)
-  const int half = pair & 1;
-  const int q_row0 = ((pair >> 1) * 2 + static_cast<int>(rank)) * BM;
-  const int n_tiles = (p.Skv + BN - 1) / BN;
+  const int cl = blockIdx.x >> 1;   // cluster index
+  const int Gc = gridDim.x >> 1;    // clusters
   const unsigned long long tmo = p.timeout_ns;
 
   if (threadIdx.x == 0) {
     mbar_init(bars + 8 * C::B_Q, 1);
+    mbar_init(bars + 8 * C::B_Q_EMPTY, 1);
     for (int s = 0; s < C::SLOTS; ++s) {
       mbar_init(bars + 8 * (C::B_KV_FULL + s), 1);
       mbar_init(bars + 8 * (C::B_KV_EMPTY + s), 1);
@@ -1433,8 +1456,10 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
     mbar_init(bars + 8 * C::B_O_FULL, 1);
     mbar_init(bars + 8 * C::B_DRAIN, 1);
     mbar_init(bars + 8 * C::B_EPI, BM);
+    mbar_init(bars + 8 * C::B_WG, BM);
     *abort_flag = 0;
     *drain_flag = 0;
+    *last_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -1457,9 +1482,11 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
     tma_prefetch_desc(&tm_v);
     tma_prefetch_desc(&tm_o);
     const uint32_t lead_q = mapa_shared(bars + 8 * C::B_Q, 0);
-    if (leader) mbar_arrive_expect_tx_warp(bars + 8 * C::B_Q, 2 * C::Q_BYTES);
-    for (int c = 0; c < 8; ++c) tma_load_3d_pair_warp(sQ + c * CHUNK_BYTES, &tm_q, lead_q, c * 64, q_row0, bh);
-    int it = 0;
+    SegIter si;
+    si.init(p, cl, Gc);
+    int unit, t0, t1;
+    bool fs;
+    int it = 0, qseg = 0;
     bool ok = true;
     auto slot_begin = [&](int& slot, uint32_t& lead_full) -> bool {
       slot = it % C::SLOTS;
@@ -1470,34 +1497,42 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
       ++it;
       return true;
     };
-    for (int j = 0; j <= n_tiles && ok; ++j) {
-      if (j < n_tiles) {
-        // K(j): keys j*128 + 64*rank .. +63, head dims 256 s .. 256 s + 255
-        for (int s = 0; s < 2 && ok; ++s) {
+    while (ok && si.next(unit, t0, t1, fs)) {
+      const Unit512 u(p, unit, rank);
+      // the Q buffer is free once this CTA's previous segment is finished with it
+      if (!bwait_warp(bars, C::B_Q_EMPTY, (qseg & 1) ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) { ok = false; break; }
+      if (leader) mbar_arrive_expect_tx_warp(bars + 8 * C::B_Q, 2 * C::Q_BYTES);
+      for (int c = 0; c < 8; ++c) tma_load_3d_pair_warp(sQ + c * CHUNK_BYTES, &tm_q, lead_q, c * 64, u.q_row0, u.bh);
+      ++qseg;
+      for (int j = t0; j <= t1 && ok; ++j) {
+        if (j < t1) {
+          // K(j): keys j*128 + 64*rank .. +63, head dims 256 s .. 256 s + 255
+          for (int s = 0; s < 2 && ok; ++s) {
+            int slot;
+            uint32_t lf;
+            if (!(ok = slot_begin(slot, lf))) break;
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+              tma_load_3d_pair_warp(sRing + slot * C::SLOT_BYTES + b * 8192, &tm_k, lf, 256 * s + 64 * b,
+                                    j * BN + 64 * static_cast<int>(rank), u.bh);
+          }
+        }
+        if (j > t0 && ok) {
+          // V(j-1): keys (j-1)*128 .. +127, head dims 256 half + 128 rank .. +127
           int slot;
           uint32_t lf;
           if (!(ok = slot_begin(slot, lf))) break;
 #pragma unroll
-          for (int b = 0; b < 4; ++b)
-            tma_load_3d_pair_warp(sRing + slot * C::SLOT_BYTES + b * 8192, &tm_k, lf, 256 * s + 64 * b,
-                                  j * BN + 64 * static_cast<int>(rank), bh);
+          for (int b = 0; b < 2; ++b)
+            tma_load_3d_pair_warp(sRing + slot * C::SLOT_BYTES + b * CHUNK_BYTES, &tm_v, lf,
+                                  C::DH * u.half + 128 * static_cast<int>(rank) + 64 * b, (j - 1) * BN, u.bh);
         }
-      }
-      if (j > 0 && ok) {
-        // V(j-1): keys (j-1)*128 .. +127, head dims 256 half + 128 rank .. +127
-        int slot;
-        uint32_t lf;
-        if (!(ok = slot_begin(slot, lf))) break;
-#pragma unroll
-        for (int b = 0; b < 2; ++b)
-          tma_load_3d_pair_warp(sRing + slot * C::SLOT_BYTES + b * CHUNK_BYTES, &tm_v, lf,
-                                256 * half + 128 * static_cast<int>(rank) + 64 * b, (j - 1) * BN, bh);
       }
     }
     if (!ok && leader) {
       // Drain: every load issued must land before shared memory goes away.
-      if (!mbar_try_wait(bars + 8 * C::B_Q, 0))
-        wait_slow(bars + 8 * C::B_Q, 0, drain_flag, 100000000ull, C::B_Q, ROLE_PRODUCER);
+      if (qseg > 0 && !mbar_try_wait(bars + 8 * C::B_Q, (qseg - 1) & 1))
+        wait_slow(bars + 8 * C::B_Q, (qseg - 1) & 1, drain_flag, 100000000ull, C::B_Q, ROLE_PRODUCER);
       const int first = it > C::SLOTS ? it - C::SLOTS : 0;
       for (int t = first; t < it; ++t) {
         const int slot = t % C::SLOTS;
@@ -1510,16 +1545,15 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
     __syncwarp();
   } else if (warp == 5 && leader) {
     // ----------------------------------------------------------- MMA issuer
-    constexpr uint32_t IDESC_QK = idesc_f16_f32(2 * BM, BN, 0, 0);   // M = 256 over the pair, N = 128 keys
-    constexpr uint32_t IDESC_PV = idesc_f16_f32(2 * BM, 256, 0, 1);  // N = 256 head dims of this half
+    constexpr uint32_t IDESC_QK = idesc_f16_f32(2 * BM, BN, 0, 0);     // M = 256 over the pair, N = 128 keys
+    constexpr uint32_t IDESC_PV = idesc_f16_f32(2 * BM, C::DH, 0, 1);  // N = 256 head dims of this half
     const uint64_t dQ = sdesc_sw128(sQ, 16, 1024);
     const uint64_t dK = sdesc_sw128(sRing, 16, 1024);             // K-major [64 keys x 64 dims] boxes
     const uint64_t dV = sdesc_sw128(sRing, CHUNK_BYTES, 1024);    // MN-major, 64-dim blocks 16 KiB apart
     const uint32_t tO = tmem + 256;
     constexpr uint16_t BOTH = 0x3;
-    int it = 0;
-    bool ok = bwait_warp(bars, C::B_Q, 0, abort_flag, tmo, ROLE_MMA);
-    tc_fence_after();
+    int it = 0, qseg = 0;
+    uint32_t gs = 0;  // S tiles issued (S / P buffer and phase)
     auto next_slot = [&](int& slot) -> bool {
       slot = it % C::SLOTS;
       const uint32_t ph = (it / C::SLOTS) & 1;
@@ -1528,8 +1562,8 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
       tc_fence_after();
       return true;
     };
-    auto issue_s = [&](int j) -> bool {
-      const uint32_t tS = tmem + 128 * (j & 1);
+    auto issue_s = [&](uint32_t g) -> bool {
+      const uint32_t tS = tmem + 128 * (g & 1);
       for (int s = 0; s < 2; ++s) {
         int slot;
         if (!next_slot(slot)) return false;
@@ -1544,13 +1578,15 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
         }
         tc_commit_pair_mc_warp(bars + 8 * (C::B_KV_EMPTY + slot), BOTH);
       }
-      tc_commit_pair_mc_warp(bars + 8 * (C::B_S_FULL + (j & 1)), BOTH);
+      tc_commit_pair_mc_warp(bars + 8 * (C::B_S_FULL + (g & 1)), BOTH);
       return true;
     };
-    auto issue_pv = [&](int j) -> bool {
-      if (!bwait_cluster_warp(bars, C::B_P_FULL + (j & 1), (j >> 1) & 1, abort_flag, tmo, ROLE_MMA)) return false;
+    // PV of S tile g; acc: accumulate into O (not the segment's first key tile);
+    // last: the segment's last key tile (O_FULL instead of PV_DONE)
+    auto issue_pv = [&](uint32_t g, bool acc, bool last) -> bool {
+      if (!bwait_cluster_warp(bars, C::B_P_FULL + (g & 1), (g >> 1) & 1, abort_flag, tmo, ROLE_MMA)) return false;
       tc_fence_after();
-      const uint32_t tP = tmem + 128 * (j & 1);
+      const uint32_t tP = tmem + 128 * (g & 1);
       int slot;
       if (!next_slot(slot)) return false;
       const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
@@ -1558,19 +1594,28 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
       for (int c = 0; c < 2; ++c) {
         // keys 64 c .. 64 c + 63: P columns 32 c .., V rows 2048 bytes per 16 keys
         const uint64_t vb = dV + soff + (static_cast<uint32_t>(4 * c * 2048) >> 4);
-        mma4_ts_pair_warp(tO, tP + 32 * c, vb, vb + 128, vb + 256, vb + 384, IDESC_PV, (j > 0 || c > 0) ? 1u : 0u);
+        mma4_ts_pair_warp(tO, tP + 32 * c, vb, vb + 128, vb + 256, vb + 384, IDESC_PV, (acc || c > 0) ? 1u : 0u);
       }
       tc_commit_pair_mc_warp(bars + 8 * (C::B_KV_EMPTY + slot), BOTH);
-      tc_commit_pair_mc_warp(bars + 8 * C::B_PV_DONE, BOTH);
+      tc_commit_pair_mc_warp(bars + 8 * (last ? C::B_O_FULL : C::B_PV_DONE), BOTH);
       return true;
     };
-    for (int j = 0; j <= n_tiles && ok; ++j) {
-      if (j < n_tiles) ok = issue_s(j);
-      if (ok && j > 0) ok = issue_pv(j - 1);
+    SegIter si;
+    si.init(p, cl, Gc);
+    int unit, t0, t1;
+    bool fs;
+    bool ok = true;
+    while (ok && si.next(unit, t0, t1, fs)) {
+      if (!bwait_warp(bars, C::B_Q, qseg & 1, abort_flag, tmo, ROLE_MMA)) { ok = false; break; }
+      ++qseg;
+      tc_fence_after();
+      const uint32_t g0 = gs;
+      for (int j = t0; j <= t1 && ok; ++j) {
+        if (j < t1) ok = issue_s(gs++);
+        if (ok && j > t0) ok = issue_pv(g0 + (j - 1 - t0), j - 1 > t0, j == t1);
+      }
     }
-    if (ok) {
-      tc_commit_pair_mc_warp(bars + 8 * C::B_O_FULL, BOTH);
-    } else {
+    if (!ok) {
       tc_commit_pair_mc_warp(bars + 8 * C::B_DRAIN, 0x1);
       wait_slow(bars + 8 * C::B_DRAIN, 0, drain_flag, 100000000ull, C::B_DRAIN, ROLE_MMA);
     }
@@ -1583,88 +1628,226 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
     const float sl2 = p.scale_log2;
     const bool pos = sl2 >= 0.f;
     const uint32_t p_full0 = mapa_shared(bars + 8 * C::B_P_FULL, 0);  // the leader's P_FULL[0]
-    float m_run = -INFINITY, l_run = 0.f;
+    SegIter si;
+    si.init(p, cl, Gc);
+    int unit, t0, t1;
+    bool first_seg;
+    uint32_t gs = 0, pvg = 0, oseg = 0, epi = 0, wsync = 0;
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int b = j & 1;
-      const uint32_t tS = tmem + lane_off + 128 * b;
-      if (!bwait_warp(bars, C::B_S_FULL + b, (j >> 1) & 1, abort_flag, tmo, ROLE_SOFTMAX0)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t s[BN];
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + 32 * c, s + 32 * c);
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) reg_fence32(s + 32 * c);
-      const int nvalid = min(BN, p.Skv - j * BN);
-      const bool full = nvalid == BN;
-      const float mx = row_extreme(s, nvalid, full, pos);
-      const float m_new = fmaxf(m_run, mx * sl2);
-      const bool need = m_new > m_run + RESCALE_THRESHOLD;
-      float factor = 1.f;
-      if (need) {
-        factor = ex2_approx(m_run - m_new);
-        m_run = m_new;
-      }
-      l_run *= factor;
-      float lsum0, lsum1;
-      if (full)
-        row_exp_store<false>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {}, [] {});
-      else
-        row_exp_store<true>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {}, [] {});
-      l_run += lsum0 + lsum1;
-      // O may only be rescaled once PV(j-1) has completed.
-      if (j > 0) {
-        if (!bwait_warp(bars, C::B_PV_DONE, (j - 1) & 1, abort_flag, tmo, ROLE_SOFTMAX0)) { ok = false; break; }
+    auto wg_sync = [&]() -> bool {
+      mbar_arrive(bars + 8 * C::B_WG);
+      const bool r = bwait_warp(bars, C::B_WG, wsync & 1, abort_flag, tmo, ROLE_SOFTMAX0);
+      ++wsync;
+      return r;
+    };
+    while (ok && si.next(unit, t0, t1, first_seg)) {
+      const Unit512 u(p, unit, rank);
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int j = t0; j < t1; ++j) {
+        const int b = gs & 1;
+        const uint32_t tS = tmem + lane_off + 128 * b;
+        if (!bwait_warp(bars, C::B_S_FULL + b, (gs >> 1) & 1, abort_flag, tmo, ROLE_SOFTMAX0)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, need)) {
-#pragma unroll 1
-          for (int c = 0; c < 256 / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + 32 * c, o);
-            tmem_wait_ld();
-            reg_fence32(o);
+        uint32_t s[BN];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
-            tmem_st32(tO + 32 * c, o);
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + 32 * c, s + 32 * c);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) reg_fence32(s + 32 * c);
+        const int nvalid = min(BN, p.Skv - j * BN);
+        const bool full = nvalid == BN;
+        const float mx = row_extreme(s, nvalid, full, pos);
+        const float m_new = fmaxf(m_run, mx * sl2);
+        const bool need = m_new > m_run + RESCALE_THRESHOLD;
+        float factor = 1.f;
+        if (need) {
+          factor = ex2_approx(m_run - m_new);
+          m_run = m_new;
+        }
+        l_run *= factor;
+        float lsum0, lsum1;
+        if (full)
+          row_exp_store<false>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {}, [] {});
+        else
+          row_exp_store<true>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {}, [] {});
+        l_run += lsum0 + lsum1;
+        // O may only be rescaled once PV(j-1) has completed.
+        if (j > t0) {
+          if (!bwait_warp(bars, C::B_PV_DONE, pvg & 1, abort_flag, tmo, ROLE_SOFTMAX0)) { ok = false; break; }
+          ++pvg;
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+            for (int c = 0; c < C::DH / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32(tO + 32 * c, o);
+              tmem_wait_ld();
+              reg_fence32(o);
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+              tmem_st32(tO + 32 * c, o);
+            }
           }
         }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive_remote(p_full0 + 8u * b);  // the leader's P_FULL[b]
+        ++gs;
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive_remote(p_full0 + 8u * b);  // the leader's P_FULL[b] (this CTA's, on the leader)
-    }
-    const bool have_o = ok && n_tiles > 0 && bwait_warp(bars, C::B_O_FULL, 0, abort_flag, tmo, ROLE_SOFTMAX0);
-    if (have_o) {
+      if (!ok) break;
+      // -------------------------------------------------- segment epilogue
+      if (!bwait_warp(bars, C::B_O_FULL, oseg & 1, abort_flag, tmo, ROLE_SOFTMAX0)) { ok = false; break; }
+      ++oseg;
       tc_fence_after();
-      const float inv = 1.f / l_run;
+      if (t0 == 0 && t1 == p.n_tiles) {
+        // whole unit: O / l staged in the Q buffer (its last MMA completed)
+        // and written with TMA; then the buffer is released for the next Q
+        const float inv = 1.f / l_run;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[64];
-        tmem_ld32(tO + 64 * c, o);
-        tmem_ld32(tO + 64 * c + 32, o + 32);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[64];
+          tmem_ld32(tO + 64 * c, o);
+          tmem_ld32(tO + 64 * c + 32, o + 32);
+          tmem_wait_ld();
+          reg_fence32(o);
+          reg_fence32(o + 32);
+          const uint32_t rowbase = sQ + c * CHUNK_BYTES + row * 128;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t a = pack_half2(__uint_as_float(o[8 * e + 0]) * inv, __uint_as_float(o[8 * e + 1]) * inv);
+            const uint32_t bb = pack_half2(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv);
+            const uint32_t cc = pack_half2(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv);
+            const uint32_t d = pack_half2(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv);
+            st_shared_v4(rowbase + ((e ^ (row & 7)) << 4), a, bb, cc, d);
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(bars + 8 * C::B_EPI);
+        const bool epi_ok = bwait_warp(bars, C::B_EPI, epi & 1, abort_flag, tmo, ROLE_SOFTMAX0);
+        ++epi;
+        if (!epi_ok) { ok = false; break; }
+        if (warp == 0) {
+          // (the odd CTA of the last pair may hold rows past Sq only: nothing to store)
+          if (lane == 0 && u.q_row0 < p.Sq) {
+            for (int c = 0; c < 4; ++c)
+              tma_store_3d(&tm_o, sQ + c * CHUNK_BYTES, C::DH * u.half + 64 * c, u.q_row0, u.bh);
+            tma_store_commit();
+            tma_store_wait_read0();
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bars + 8 * C::B_Q_EMPTY);
+        }
+        continue;
+      }
+      // partial piece: the Q buffer is not needed for it
+      if (warp == 0 && lane == 0) mbar_arrive(bars + 8 * C::B_Q_EMPTY);
+      // unnormalised O, m and l of this CTA's rows to its workspace slot,
+      // chunk-major: [DH/4][128 rows][4] fp32
+      const int which = first_seg ? 0 : 1;
+      const long long slot = (static_cast<long long>(cl) * 2 + rank) * 2 + which;
+      float* wo = p.ws_o + slot * BM * C::DH + row * 4;
+#pragma unroll 1
+      for (int c = 0; c < C::DH / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + 32 * c, o);
         tmem_wait_ld();
         reg_fence32(o);
-        reg_fence32(o + 32);
-        // Q is dead (its last MMA completed): it becomes the staging buffer
-        const uint32_t rowbase = sQ + c * CHUNK_BYTES + row * 128;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint32_t a = pack_half2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
-          const uint32_t bb = pack_half2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
-          const uint32_t cc = pack_half2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
-          const uint32_t d = pack_half2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
-          st_shared_v4(rowbase + ((u ^ (row & 7)) << 4), a, bb, cc, d);
+        for (int e = 0; e < 8; ++e)
+          *reinterpret_cast<float4*>(wo + (c * 8 + e) * BM * 4) =
+              make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]), __uint_as_float(o[4 * e + 2]),
+                          __uint_as_float(o[4 * e + 3]));
+      }
+      *reinterpret_cast<float2*>(p.ws_ml + (slot * BM + row) * 2) = make_float2(m_run, l_run);
+      if (!wg_sync()) { ok = false; break; }
+      const int rel = unit - p.tail_unit0;
+      unsigned long long* cnt = p.ws_cnt + rel * 2 + rank;
+      const long long W = p.total_steps;
+      const int GT = p.tail_ctas;
+      const long long ubase = static_cast<long long>(rel) * p.n_tiles;
+      const int c_lo = owner_cta(ubase, W, GT);
+      const int c_hi = owner_cta(ubase + p.n_tiles - 1, W, GT);
+      if (warp == 0 && lane == 0) {
+        __threadfence();
+        unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(cnt), next;
+        while (true) {
+          next = (((cur >> 8) == p.epoch) ? cur : (p.epoch << 8)) + 1ull;
+          const unsigned long long seen = atomicCAS(cnt, cur, next);
+          if (seen == cur) break;
+          cur = seen;
+        }
+        const int last = (static_cast<int>(next & 0xffull) == c_hi - c_lo + 1) ? 1 : 0;
+        if (last) __threadfence();
+        *last_flag = last;
+      }
+      if (!wg_sync()) { ok = false; break; }
+      if (!*last_flag) continue;
+      // Last piece to finish: combine every piece of this (unit, rank) in
+      // cluster order (deterministic bits) and store the rows directly.
+      const int np = c_hi - c_lo + 1;
+      auto piece_row = [&](int k) -> long long {
+        const int c2 = c_lo + k;
+        const int which2 = (static_cast<long long>(c2) * W >= ubase * GT) ? 0 : 1;
+        return ((static_cast<long long>(c2) * 2 + rank) * 2 + which2) * BM + row;
+      };
+      auto piece_ml = [&](long long rb) -> float2 {
+        return __ldcg(reinterpret_cast<const float2*>(p.ws_ml + rb * 2));
+      };
+      float m_all = -INFINITY;
+#pragma unroll 1
+      for (int k = 0; k < np; ++k) m_all = fmaxf(m_all, piece_ml(piece_row(k)).x);
+      float l_all = 0.f;
+#pragma unroll 1
+      for (int k = 0; k < np; ++k) {
+        const float2 ml = piece_ml(piece_row(k));
+        l_all = fmaf(ml.y, ex2_approx(ml.x - m_all), l_all);
+      }
+      const float inv = 1.f / l_all;
+      const int grow = u.q_row0 + row;
+      __half* orow = p.o + (static_cast<long long>(u.bh) * p.Sq + grow) * 512 + C::DH * u.half;
+#pragma unroll 1
+      for (int c = 0; c < C::DH / 32; ++c) {
+        float acc[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+#pragma unroll 1
+        for (int k0 = 0; k0 < np; k0 += 2) {
+          float4 v4[2][8];
+          float wk[2];
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk) {
+            const int k = (k0 + kk < np) ? k0 + kk : k0;  // a duplicate load, never accumulated
+            const long long rb = piece_row(k);
+            wk[kk] = ex2_approx(piece_ml(rb).x - m_all);
+            const long long sl = rb / BM;
+            const float* sbase = p.ws_o + sl * BM * C::DH + (rb - sl * BM) * 4;
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              v4[kk][e] = __ldcg(reinterpret_cast<const float4*>(sbase + (c * 8 + e) * BM * 4));
+          }
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk) {
+            if (k0 + kk < np) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                acc[4 * e] = fmaf(v4[kk][e].x, wk[kk], acc[4 * e]);
+                acc[4 * e + 1] = fmaf(v4[kk][e].y, wk[kk], acc[4 * e + 1]);
+                acc[4 * e + 2] = fmaf(v4[kk][e].z, wk[kk], acc[4 * e + 2]);
+                acc[4 * e + 3] = fmaf(v4[kk][e].w, wk[kk], acc[4 * e + 3]);
+              }
+            }
+          }
+        }
+        if (grow < p.Sq) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            *reinterpret_cast<uint4*>(orow + 32 * c + 8 * e) =
+                make_uint4(pack_half2(acc[8 * e] * inv, acc[8 * e + 1] * inv),
+                           pack_half2(acc[8 * e + 2] * inv, acc[8 * e + 3] * inv),
+                           pack_half2(acc[8 * e + 4] * inv, acc[8 * e + 5] * inv),
+                           pack_half2(acc[8 * e + 6] * inv, acc[8 * e + 7] * inv));
         }
       }
-      fence_proxy_async_smem();
-    }
-    mbar_arrive(bars + 8 * C::B_EPI);
-    // (the odd CTA of the last pair may hold rows past Sq only: nothing to store)
-    if (warp == 0 && lane == 0 && have_o && q_row0 < p.Sq && bwait(bars, C::B_EPI, 0, abort_flag, tmo, ROLE_SOFTMAX0)) {
-      for (int c = 0; c < 4; ++c) tma_store_3d(&tm_o, sQ + c * CHUNK_BYTES, 256 * half + 64 * c, q_row0, bh);
-      tma_store_commit();
-      tma_store_wait_read0();
     }
   }
 
@@ -2010,10 +2193,61 @@ int launch_d512(const void* q, const void* k, const void* v, void* o, long long 
   return GFX906_B200_OK;
 }
 
-// D = 512 (row-major) on CTA pairs: grid x = 2 CTAs x 2 head-dim halves x
-// ceil(query tiles / 2) pairs, clusters of 2 along x.
-int launch_d512_pair(const void* q, const void* k, const void* v, void* o, long long BH, int Sq, int Skv, float scale,
-                     cudaStream_t stream) {
+// Persistent schedule of attn_fwd_d512_pair_kernel: units are (batch x head,
+// query-tile pair, head-dim half), one cluster of two CTAs per SM pair.
+// Whole units first; with a workspace, the last partial wave's key range is
+// split over the clusters (units of >= kMinSplitTiles512 key tiles) when
+// there are fewer units than clusters or the partial wave is at most half
+// full. Measured on B200 (TFLOP/s, whole -> split): one 8-GPU rank's row shard
+// of C4 (1x4x512x4096, 16 units) 217 -> 307, a 4-GPU shard 442 -> 551; C4
+// itself (128 units, a partial wave of 54 on 74 clusters) 877 -> 849, so it
+// runs whole units.
+constexpr int kMinSplitTiles512 = 8;
+
+bool make_plan512(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Plan* pl) {
+  const long long npairs = ((Sq + fa::BM - 1) / fa::BM + 1) / 2;
+  pl->n_qb = static_cast<int>(2 * npairs);  // units per (batch, head)
+  pl->unit_rows = 2 * fa::BM;
+  pl->n_tiles = (Skv + fa::BN - 1) / fa::BN;
+  const long long U = 2 * npairs * BH;
+  if (U > 0x7fffffffll) return false;
+  pl->n_units = static_cast<int>(U);
+  const long long G = num_sms / 2 > 0 ? num_sms / 2 : 1;  // clusters
+  const long long waves = U / G;
+  const long long tail = U - waves * G;
+  pl->split = (allow_split && tail > 0 && pl->n_tiles >= kMinSplitTiles512 && (waves == 0 || 2 * tail <= G)) ? 1 : 0;
+  if (pl->split) {
+    pl->tail_unit0 = static_cast<int>(waves * G);
+    pl->total_steps = tail * pl->n_tiles;
+    long long gt = (pl->total_steps + kMinSplitSteps - 1) / kMinSplitSteps;
+    if (gt > G) gt = G;
+    if (gt > (fa::MAX_PIECES - 1) * tail) gt = (fa::MAX_PIECES - 1) * tail;
+    pl->tail_ctas = static_cast<int>(gt);
+    pl->G = static_cast<int>(waves > 0 ? G : gt);
+  } else {
+    pl->tail_unit0 = pl->n_units;
+    pl->tail_ctas = 0;
+    pl->total_steps = 0;
+    pl->G = static_cast<int>(U < G ? U : G);
+  }
+  return true;
+}
+
+// Workspace of a split D = 512 plan: [counters (unit, rank)][partial (m, l)]
+// [partial O], slots of 128 rows x 256 fp32 per (cluster, rank, piece).
+size_t workspace_bytes512(const Plan& pl) {
+  if (!pl.split) return 0;
+  const size_t slots = static_cast<size_t>(pl.tail_ctas) * 2 * 2 * fa::BM;
+  return align256(static_cast<size_t>(pl.n_units - pl.tail_unit0) * 2 * sizeof(unsigned long long)) +
+         align256(slots * 2 * sizeof(float)) + slots * fa::Cfg512P::DH * sizeof(float);
+}
+
+// D = 512 (row-major) on CTA pairs: grid x = 2 x clusters, clusters of 2.
+int launch_d512_pair(const void* q, const void* k, const void* v, void* o, long long BH, int Sq, int Skv,
+                     float scale, void* ws, size_t ws_size, int dev, cudaStream_t stream) {
+  Plan pl;
+  if (!make_plan512(BH, Sq, Skv, device_sms(dev), ws != nullptr, &pl)) return GFX906_B200_EINVAL;
+  if (BH > 0x7fffffffll) return GFX906_B200_EINVAL;
   CUtensorMap mq, mk, mv, mo;
   if (!make_map(&mq, q, 512, Sq, BH, fa::BM) || !make_map(&mk, k, 512, Skv, BH, fa::BN / 2) ||
       !make_map(&mv, v, 512, Skv, BH, fa::BN) || !make_map(&mo, o, 512, Sq, BH, fa::BM))
@@ -2022,19 +2256,32 @@ int launch_d512_pair(const void* q, const void* k, const void* v, void* o, long 
   prm.Sq = Sq;
   prm.Skv = Skv;
   prm.D = 512;
+  prm.bh_offset = 0;
   prm.scale_log2 = scale * 1.4426950408889634f;
   prm.timeout_ns = timeout_ns_from_env();
-  const long long qtiles = (Sq + fa::BM - 1) / fa::BM;
-  const long long gx = 4 * ((qtiles + 1) / 2);
-  if (gx > 0x7fffffffll) return GFX906_B200_EINVAL;
-  for (long long off = 0; off < BH; off += 65535) {
-    const long long n = (BH - off) < 65535 ? (BH - off) : 65535;
-    prm.bh_offset = static_cast<int>(off);
-    const int rc = launch_pdl(fa::attn_fwd_d512_pair_kernel, dim3(static_cast<unsigned>(gx), static_cast<unsigned>(n), 1),
-                              dim3(fa::Cfg512P::THREADS), fa::Cfg512P::SMEM_BYTES, stream, 2, mq, mk, mv, mo, prm);
-    if (rc != GFX906_B200_OK) return rc;
+  prm.n_qb = pl.n_qb;
+  prm.unit_rows = pl.unit_rows;
+  prm.n_units = pl.n_units;
+  prm.n_tiles = pl.n_tiles;
+  prm.split = pl.split;
+  prm.tail_unit0 = pl.tail_unit0;
+  prm.tail_ctas = pl.tail_ctas;
+  prm.total_steps = pl.total_steps;
+  prm.o = static_cast<__half*>(o);
+  if (pl.split) {
+    const size_t need = workspace_bytes512(pl);
+    if (ws_size < need || (reinterpret_cast<uintptr_t>(ws) & 255u)) return GFX906_B200_EINVAL;
+    uint8_t* base = static_cast<uint8_t*>(ws);
+    const size_t slots = static_cast<size_t>(pl.tail_ctas) * 2 * 2 * fa::BM;
+    prm.ws_cnt = reinterpret_cast<unsigned long long*>(base);
+    base += align256(static_cast<size_t>(pl.n_units - pl.tail_unit0) * 2 * sizeof(unsigned long long));
+    prm.epoch = next_epoch();
+    prm.ws_ml = reinterpret_cast<float*>(base);
+    base += align256(slots * 2 * sizeof(float));
+    prm.ws_o = reinterpret_cast<float*>(base);
   }
-  return GFX906_B200_OK;
+  return launch_pdl(fa::attn_fwd_d512_pair_kernel, dim3(2 * static_cast<unsigned>(pl.G)), dim3(fa::Cfg512P::THREADS),
+                    fa::Cfg512P::SMEM_BYTES, stream, 2, mq, mk, mv, mo, prm);
 }
 
 // Argument checks shared by every entry point. Returns OK and sets *skip when
@@ -2077,7 +2324,7 @@ int attn_launch_impl(const void* q, const void* k, const void* v, void* o, int B
   }
   if (D == 128) return launch_dp<128>(q, k, v, o, BH, Sq, Skv, D, scale, ws, ws_size, dev, stream);
   if (D <= 64) return launch_dp<64>(q, k, v, o, BH, Sq, Skv, D, scale, ws, ws_size, dev, stream);
-  return launch_d512_pair(q, k, v, o, BH, Sq, Skv, scale, stream);
+  return launch_d512_pair(q, k, v, o, BH, Sq, Skv, scale, ws, ws_size, dev, stream);
 }
 
 }  // namespace
@@ -2124,10 +2371,14 @@ size_t gfx906_b200_attn_workspace_size(int B, int H, int Sq, int Skv, int D) {
   const int probe = 16;  // any aligned non-null value: only sizes are checked here
   const void* fake = reinterpret_cast<const void*>(static_cast<uintptr_t>(probe));
   if (check_args(fake, fake, fake, fake, B, H, Sq, Skv, D, &skip) != GFX906_B200_OK || skip) return 0;
-  if (Skv == 0 || D == 512) return 0;
+  if (Skv == 0) return 0;
   int dev = 0;
   if (check_device(&dev) != GFX906_B200_OK) return 0;
   Plan pl;
+  if (D == 512) {
+    if (!make_plan512(static_cast<long long>(B) * H, Sq, Skv, device_sms(dev), true, &pl)) return 0;
+    return workspace_bytes512(pl);
+  }
   if (!make_plan(static_cast<long long>(B) * H, Sq, Skv, device_sms(dev), true, &pl)) return 0;
   return workspace_bytes(pl, D == 128 ? 128 : 64);
 }
@@ -2147,13 +2398,16 @@ int gfx906_b200_attn_plan(int B, int H, int Sq, int Skv, int D, int with_workspa
     num_sms = device_sms(dev);
   }
   const long long BH = static_cast<long long>(B) * H;
+  Plan pl;
   if (D == 512) {
-    const long long ctas = 4ll * (((Sq + fa::BM - 1) / fa::BM + 1) / 2) * BH;
-    out4[0] = static_cast<int>(ctas < 0x7fffffffll ? ctas : 0x7fffffffll);
-    out4[3] = fa::BM;
+    // CTAs (2 per cluster); unit_rows = query rows of a unit (a pair of tiles)
+    if (!make_plan512(BH, Sq, Skv, num_sms, with_workspace != 0, &pl)) return GFX906_B200_EINVAL;
+    out4[0] = 2 * pl.G;
+    out4[1] = pl.split;
+    out4[2] = 2 * pl.tail_ctas;
+    out4[3] = pl.unit_rows;
     return GFX906_B200_OK;
   }
-  Plan pl;
   if (!make_plan(BH, Sq, Skv, num_sms, with_workspace != 0, &pl)) return GFX906_B200_EINVAL;
   out4[0] = pl.G;
   out4[1] = pl.split;

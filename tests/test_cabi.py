@@ -107,8 +107,15 @@ def test_plan_short_units(lib):
     # C2: the partial last wave of 32-key-tile units is split
     pl = plan(lib, 1, 24, 4096, 4096, 128)
     assert pl["split"] == 1 and pl["ctas"] == 148
-    # D=512: two head-dim halves per 128-row query tile, never split
-    assert plan(lib, 1, 4, 4096, 4096, 512) == {"ctas": 256, "split": 0, "tail_ctas": 0, "unit_rows": 128}
+    # D=512 on CTA pairs: C4's 128 units (query-tile pairs x head-dim halves)
+    # run whole on 74 clusters; one 8-GPU rank's shard of C4 (16 units) is split
+    # over all 74
+    for ws in (True, False):
+        assert plan(lib, 1, 4, 4096, 4096, 512, ws=ws) == {"ctas": 148, "split": 0, "tail_ctas": 0, "unit_rows": 256}
+    assert plan(lib, 1, 4, 512, 4096, 512) == {"ctas": 148, "split": 1, "tail_ctas": 148, "unit_rows": 256}
+    assert plan(lib, 1, 4, 512, 4096, 512, ws=False)["ctas"] == 32
+    # 4 units of one key tile: whole units, one cluster each
+    assert plan(lib, 1, 1, 256, 100, 512) == {"ctas": 4, "split": 0, "tail_ctas": 0, "unit_rows": 256}
 
 
 def test_plan_argument_checks(lib):

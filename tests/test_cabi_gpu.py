@@ -65,7 +65,9 @@ def test_schedules_match_oracle(lib, shape, use_ws):
 
 
 def test_workspace_size_and_checks(lib):
-    assert lib.workspace_size(1, 4, 1024, 1024, 512) == 0  # D=512 never splits
+    assert lib.workspace_size(1, 1, 256, 100, 512) == 0  # D=512, one key tile: whole units
+    assert lib.workspace_size(1, 4, 4096, 4096, 512) == 0  # D=512, C4: whole units on 74 clusters
+    assert lib.workspace_size(1, 4, 512, 4096, 512) > 0  # D=512, 16 units < 74 clusters: split
     assert lib.workspace_size(1, 4, 1024, 0, 64) == 0
     assert lib.workspace_size(1, 4, 1024, 1024, 100) == 0
     assert lib.workspace_size(2, 16, 4096, 1024, 128) == 0  # 8 key tiles per unit: never split

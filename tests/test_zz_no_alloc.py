@@ -28,8 +28,8 @@ pytestmark = pytest.mark.gpu
 # that do not split (no scratch: the call forwards to the workspace entry
 # with none).
 SPLIT_SHAPES = [(1, 1, 16384, 16384, 64), (1, 3, 300, 2000, 128), (1, 4, 16384, 16384, 128),
-                (1, 1, 4096, 32768, 64)]
-WHOLE_SHAPES = [(2, 16, 4096, 1024, 128), (1, 8, 1024, 1024, 64), (1, 2, 1024, 1024, 512)]
+                (1, 1, 4096, 32768, 64), (1, 2, 1024, 1024, 512), (1, 4, 512, 4096, 512)]
+WHOLE_SHAPES = [(2, 16, 4096, 1024, 128), (1, 8, 1024, 1024, 64), (1, 1, 256, 100, 512), (1, 4, 4096, 4096, 512)]
 
 
 @pytest.fixture(scope="module")
