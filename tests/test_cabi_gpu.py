@@ -17,7 +17,12 @@ pytestmark = pytest.mark.gpu
 
 SHAPES = [(1, 8, 1024, 1024, 64), (1, 24, 4096, 4096, 128), (2, 16, 4096, 1024, 128),
           (1, 1, 16384, 16384, 64), (1, 3, 300, 2000, 128), (3, 5, 777, 1500, 32),
-          (1, 2, 100, 129, 128), (1, 1, 129, 5000, 16)]
+          (1, 2, 100, 129, 128), (1, 1, 129, 5000, 16),
+          # D = 512 on CTA pairs: C4 (whole units over 74 clusters), one 8-GPU
+          # rank's shard of C4 (16 units: split with a workspace), an odd
+          # number of query tiles (the last pair's odd CTA past Sq), ragged keys
+          (1, 4, 4096, 4096, 512), (1, 4, 512, 4096, 512), (1, 1, 384, 1000, 512), (3, 5, 640, 2000, 512),
+          (2, 4, 77, 411, 512)]
 
 
 @pytest.fixture(scope="module")
