@@ -260,7 +260,9 @@ def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, 
     whole 256-row blocks, K and V broadcast from rank 0 with NCCL, O gathered
     with all_gather_into_tensor (gfx906_b200.shard.attention_by_rows). Times,
     each the max over ranks of CUDA events on the launching stream: the kernel
-    alone, the broadcast alone, the gather alone, and the three together."""
+    alone, the broadcast alone, the gather alone, the three in sequence, and
+    the three pipelined across calls (the next call's K/V broadcast overlapping
+    this call's kernel, gathers asynchronous)."""
     import gfx906_b200
     from gfx906_b200 import shard
 
@@ -284,24 +286,44 @@ def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, 
         if world > 1:
             shard._gather_dim(local_out, counts, 2, None, out=out_full)
 
+    # pipelined: every call still broadcasts its K/V, runs the kernel and
+    # gathers its O, but the next call's broadcast (other buffers) runs on the
+    # collective stream while this call's kernel runs, and the gathers are
+    # asynchronous
+    kbuf, vbuf = [kd, kd.clone()], [vd, vd.clone()]
+    obuf = [out_full, torch.empty_like(out_full)]
+
+    def pipelined(n):
+        pending = shard.broadcast_kv(kbuf[0], vbuf[0], src=0, async_op=True)
+        gathers = []
+        for i in range(n):
+            for w in pending:
+                w.wait()
+            if i + 1 < n:
+                pending = shard.broadcast_kv(kbuf[(i + 1) % 2], vbuf[(i + 1) % 2], src=0, async_op=True)
+            local = gfx906_b200.attn(q_rows, kbuf[i % 2], vbuf[i % 2], cfg.scale)
+            gathers.append(shard.gather_rows(local, cfg.Sq, obuf[i % 2], async_op=True))
+        for w in gathers:
+            if w is not None:
+                w.wait()
+
     legs = {
-        "kernel": lambda: gfx906_b200.attn(q_rows, kd, vd, cfg.scale),
-        "broadcast": bcast,
-        "gather": gather,
-        "with_collectives": lambda: shard.attention_by_rows(q_rows, kd, vd, cfg.scale, cfg.Sq, src=0,
-                                                            out=out_full),
+        "kernel": (lambda n: [gfx906_b200.attn(q_rows, kd, vd, cfg.scale) for _ in range(n)]),
+        "broadcast": (lambda n: [bcast() for _ in range(n)]),
+        "gather": (lambda n: [gather() for _ in range(n)]),
+        "with_collectives": (lambda n: [shard.attention_by_rows(q_rows, kd, vd, cfg.scale, cfg.Sq, src=0,
+                                                                out=out_full) for _ in range(n)]),
+        "pipelined": pipelined,
     }
     ms = {}
     for name, fn in legs.items():  # every rank runs the same legs in the same order
-        for _ in range(max(3, warmup)):  # NCCL's lazy set-up stays out of the timing
-            fn()
+        fn(max(3, warmup))  # NCCL's lazy set-up stays out of the timing
         torch.cuda.synchronize()
         barrier(world)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(steps):
-            fn()
+        fn(steps)
         e1.record(stream)
         torch.cuda.synchronize()
         barrier(world)
@@ -312,9 +334,10 @@ def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, 
         "workload": f"{cfg.name}: {cfg.describe()}",
         "ranks": world, "rows_per_rank": sh.size, "steps": steps,
         "kernel_ms": ms["kernel"], "broadcast_ms": ms["broadcast"], "gather_ms": ms["gather"],
-        "with_collectives_ms": ms["with_collectives"],
+        "with_collectives_ms": ms["with_collectives"], "pipelined_ms": ms["pipelined"],
         "value_kernel": cfg.flops / (ms["kernel"] * 1e-3) / 1e12,
         "value_with_collectives": cfg.flops / (ms["with_collectives"] * 1e-3) / 1e12,
+        "value_pipelined": cfg.flops / (ms["pipelined"] * 1e-3) / 1e12,
         "unit": UNIT,
         "collectives": (f"NCCL broadcast of K and V from rank 0 ({kv_bytes / 2**20:.0f} MiB) and "
                         f"all_gather_into_tensor of O ({o_bytes / 2**20:.0f} MiB) over {world} rank(s)"

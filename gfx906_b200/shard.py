@@ -164,6 +164,41 @@ def attention_by_rows(q_rows, k, v, scale, Sq: int, src: Optional[int] = 0, grou
     return _gather_dim(local, counts, 2, group, out=out)
 
 
+def broadcast_kv(k, v, src: int = 0, group=None, async_op: bool = False):
+    """Replicate K and V from rank `src` (one NCCL broadcast each).
+
+    With async_op the broadcasts are enqueued on the collective stream after
+    the work already issued on the current stream, and a list of two work
+    handles is returned; `wait()` on them makes the current stream wait. A
+    caller can so broadcast the next call's K/V while this call's kernel runs
+    (the kernel reads other buffers)."""
+    world, _ = _group_world(group)
+    if world == 1:
+        return []
+    wk = dist.broadcast(k, src=src, group=group, async_op=async_op)
+    wv = dist.broadcast(v, src=src, group=group, async_op=async_op)
+    return [wk, wv] if async_op else []
+
+
+def gather_rows(local, Sq: int, out: torch.Tensor, group=None, async_op: bool = False):
+    """All-gather the ranks' query-row blocks of O into `out` ([B, H, Sq, D]).
+
+    Equal blocks with B * H == 1 (C5 on 1/2/4/8 GPUs) go through one
+    all_gather_into_tensor straight into `out`; with async_op its work
+    handle is returned (None otherwise, or when the gather had to run
+    synchronously through the padded path)."""
+    world, rank = _group_world(group)
+    if world == 1:
+        out.copy_(local)
+        return None
+    counts = [row_shard(Sq, r, world).size for r in range(world)]
+    outer = local.shape[0] * local.shape[1]
+    if async_op and len(set(counts)) == 1 and outer == 1 and local.is_contiguous() and out.is_contiguous():
+        return dist.all_gather_into_tensor(out.view(-1), local.view(-1), group=group, async_op=True)
+    _gather_dim(local, counts, 2, group, out=out)
+    return None
+
+
 def choose_partition(B: int, H: int, world: int) -> str:
     """"heads" while every rank gets at least one (batch x head) unit, else "rows"."""
     return "heads" if B * H >= world else "rows"

@@ -50,6 +50,9 @@ def _worker(rank, world, port, mode, result_q):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
+        if mode == "pipelined":
+            _pipelined(rank, world, result_q)
+            return
         B, H, Sq, Skv, D = {"heads": (2, 3, 300, 257, 64), "rows": (1, 1, 1100, 700, 64),
                             "rows_eq": (1, 1, 256 * world * 2, 700, 64), "rows_bh": (2, 3, 512 * world, 300, 32),
                             "auto": (1, 2, 800, 300, 32)}[mode]
@@ -77,8 +80,48 @@ def _worker(rank, world, port, mode, result_q):
         dist.destroy_process_group()
 
 
+def _pipelined(rank, world, result_q):
+    """Three calls with the next call's K/V broadcast while this one computes,
+    and each output gathered asynchronously; every output must equal the
+    unsharded result of its own inputs."""
+    Sq, Skv, D = 256 * world * 2, 300, 64
+    scale = D ** -0.5
+    inputs = [make_qkv(1, 1, Sq, Skv, D, seed=20 + i) for i in range(3)]
+    sh = shard.row_shard(Sq, rank, world)
+    kbuf = [torch.zeros(1, 1, Skv, D, dtype=torch.float16) for _ in range(2)]
+    vbuf = [torch.zeros(1, 1, Skv, D, dtype=torch.float16) for _ in range(2)]
+    outs = [torch.full((1, 1, Sq, D), float("nan"), dtype=torch.float16) for _ in range(3)]
+
+    def load(i):
+        if rank == 0:
+            kbuf[i % 2].copy_(inputs[i][1])
+            vbuf[i % 2].copy_(inputs[i][2])
+        return shard.broadcast_kv(kbuf[i % 2], vbuf[i % 2], src=0, async_op=True)
+
+    pending = load(0)
+    gathers = []
+    for i in range(3):
+        for w in pending:
+            w.wait()
+        if i + 1 < 3:
+            pending = load(i + 1)
+        q_rows = inputs[i][0][:, :, sh.start:sh.stop].contiguous()
+        local = oracle_attn(q_rows, kbuf[i % 2].clone(), vbuf[i % 2].clone(), scale)
+        gathers.append(shard.gather_rows(local, Sq, outs[i], async_op=True))
+    for w in gathers:
+        if w is not None:
+            w.wait()
+    if rank == 0:
+        err = 0.0
+        for i in range(3):
+            q, k, v = inputs[i]
+            err = max(err, float((outs[i].float() - oracle_attn(q, k, v, scale).float()).abs().max()))
+        result_q.put(err)
+
+
 @pytest.mark.parametrize("mode,world", [("heads", 2), ("rows", 2), ("rows", 3), ("heads", 3), ("auto", 2),
-                                        ("auto", 3), ("rows_eq", 2), ("rows_eq", 3), ("rows_bh", 2)])
+                                        ("auto", 3), ("rows_eq", 2), ("rows_eq", 3), ("rows_bh", 2),
+                                        ("pipelined", 2), ("pipelined", 3)])
 def test_sharded_attention_matches_unsharded(mode, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
