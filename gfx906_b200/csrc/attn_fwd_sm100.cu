@@ -115,7 +115,8 @@ struct Params {
   __half* o;              // output, [B*H, Sq, D] fp16
   float* ws_o;            // split workspace: [tail_ctas][2][2] slots of [DP/4][128][4] partial O
   float* ws_ml;           // [tail_ctas][2][2][128][2] partial (m, l)
-  unsigned long long* ws_cnt;  // [tail units][2] arrival counters: (epoch << 8) | arrivals
+  int combine;            // 1: the last piece of a unit combines it in the kernel (D <= 128)
+  unsigned long long* ws_cnt;  // [tail units][2] arrival counters: (epoch << 8) | arrivals (combine == 1)
   unsigned long long epoch;    // unique per launch (56 bits), tags the counters
 };
 
@@ -878,6 +879,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
       }
       *reinterpret_cast<float2*>(wml) = make_float2(m_run, l_run);
+      // Units of few pieces are combined here by the piece that finishes
+      // last, overlapping the other CTAs' work; units of many pieces by
+      // attn_combine_kernel, launched after this grid (p.combine == 0).
+      if (!p.combine) continue;
       // Release: the warpgroup rendezvous orders every thread's stores before
       // thread 0's gpu-scope fence, which orders them before the counter.
       if (!wg_sync()) { ok = false; break; }
@@ -1364,7 +1369,7 @@ struct Cfg512P {
   static constexpr int DATA_BYTES = Q_BYTES + SLOTS * SLOT_BYTES;
   static constexpr int B_Q = 0, B_Q_EMPTY = 1, B_KV_FULL = 2, B_KV_EMPTY = 2 + SLOTS, B_S_FULL = 2 + 2 * SLOTS;
   static constexpr int B_P_FULL = B_S_FULL + 2, B_PV_DONE = B_P_FULL + 2, B_O_FULL = B_PV_DONE + 1;
-  static constexpr int B_DRAIN = B_O_FULL + 1, B_EPI = B_DRAIN + 1, B_WG = B_EPI + 1, NUM_BARS = B_WG + 1;
+  static constexpr int B_DRAIN = B_O_FULL + 1, B_EPI = B_DRAIN + 1, NUM_BARS = B_EPI + 1;
   static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 256;
   static constexpr int DH = 256;  // head dims per CTA pair (one half of D = 512)
@@ -1431,7 +1436,6 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::DATA_BYTES + C::NUM_BARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* drain_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
-  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 3);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -1456,10 +1460,8 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
     mbar_init(bars + 8 * C::B_O_FULL, 1);
     mbar_init(bars + 8 * C::B_DRAIN, 1);
     mbar_init(bars + 8 * C::B_EPI, BM);
-    mbar_init(bars + 8 * C::B_WG, BM);
     *abort_flag = 0;
     *drain_flag = 0;
-    *last_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -1632,14 +1634,8 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
     si.init(p, cl, Gc);
     int unit, t0, t1;
     bool first_seg;
-    uint32_t gs = 0, pvg = 0, oseg = 0, epi = 0, wsync = 0;
+    uint32_t gs = 0, pvg = 0, oseg = 0, epi = 0;
     bool ok = true;
-    auto wg_sync = [&]() -> bool {
-      mbar_arrive(bars + 8 * C::B_WG);
-      const bool r = bwait_warp(bars, C::B_WG, wsync & 1, abort_flag, tmo, ROLE_SOFTMAX0);
-      ++wsync;
-      return r;
-    };
     while (ok && si.next(unit, t0, t1, first_seg)) {
       const Unit512 u(p, unit, rank);
       float m_run = -INFINITY, l_run = 0.f;
@@ -1759,95 +1755,7 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
                           __uint_as_float(o[4 * e + 3]));
       }
       *reinterpret_cast<float2*>(p.ws_ml + (slot * BM + row) * 2) = make_float2(m_run, l_run);
-      if (!wg_sync()) { ok = false; break; }
-      const int rel = unit - p.tail_unit0;
-      unsigned long long* cnt = p.ws_cnt + rel * 2 + rank;
-      const long long W = p.total_steps;
-      const int GT = p.tail_ctas;
-      const long long ubase = static_cast<long long>(rel) * p.n_tiles;
-      const int c_lo = owner_cta(ubase, W, GT);
-      const int c_hi = owner_cta(ubase + p.n_tiles - 1, W, GT);
-      if (warp == 0 && lane == 0) {
-        __threadfence();
-        unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(cnt), next;
-        while (true) {
-          next = (((cur >> 8) == p.epoch) ? cur : (p.epoch << 8)) + 1ull;
-          const unsigned long long seen = atomicCAS(cnt, cur, next);
-          if (seen == cur) break;
-          cur = seen;
-        }
-        const int last = (static_cast<int>(next & 0xffull) == c_hi - c_lo + 1) ? 1 : 0;
-        if (last) __threadfence();
-        *last_flag = last;
-      }
-      if (!wg_sync()) { ok = false; break; }
-      if (!*last_flag) continue;
-      // Last piece to finish: combine every piece of this (unit, rank) in
-      // cluster order (deterministic bits) and store the rows directly.
-      const int np = c_hi - c_lo + 1;
-      auto piece_row = [&](int k) -> long long {
-        const int c2 = c_lo + k;
-        const int which2 = (static_cast<long long>(c2) * W >= ubase * GT) ? 0 : 1;
-        return ((static_cast<long long>(c2) * 2 + rank) * 2 + which2) * BM + row;
-      };
-      auto piece_ml = [&](long long rb) -> float2 {
-        return __ldcg(reinterpret_cast<const float2*>(p.ws_ml + rb * 2));
-      };
-      float m_all = -INFINITY;
-#pragma unroll 1
-      for (int k = 0; k < np; ++k) m_all = fmaxf(m_all, piece_ml(piece_row(k)).x);
-      float l_all = 0.f;
-#pragma unroll 1
-      for (int k = 0; k < np; ++k) {
-        const float2 ml = piece_ml(piece_row(k));
-        l_all = fmaf(ml.y, ex2_approx(ml.x - m_all), l_all);
-      }
-      const float inv = 1.f / l_all;
-      const int grow = u.q_row0 + row;
-      __half* orow = p.o + (static_cast<long long>(u.bh) * p.Sq + grow) * 512 + C::DH * u.half;
-#pragma unroll 1
-      for (int c = 0; c < C::DH / 32; ++c) {
-        float acc[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) acc[e] = 0.f;
-#pragma unroll 1
-        for (int k0 = 0; k0 < np; k0 += 2) {
-          float4 v4[2][8];
-          float wk[2];
-#pragma unroll
-          for (int kk = 0; kk < 2; ++kk) {
-            const int k = (k0 + kk < np) ? k0 + kk : k0;  // a duplicate load, never accumulated
-            const long long rb = piece_row(k);
-            wk[kk] = ex2_approx(piece_ml(rb).x - m_all);
-            const long long sl = rb / BM;
-            const float* sbase = p.ws_o + sl * BM * C::DH + (rb - sl * BM) * 4;
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              v4[kk][e] = __ldcg(reinterpret_cast<const float4*>(sbase + (c * 8 + e) * BM * 4));
-          }
-#pragma unroll
-          for (int kk = 0; kk < 2; ++kk) {
-            if (k0 + kk < np) {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                acc[4 * e] = fmaf(v4[kk][e].x, wk[kk], acc[4 * e]);
-                acc[4 * e + 1] = fmaf(v4[kk][e].y, wk[kk], acc[4 * e + 1]);
-                acc[4 * e + 2] = fmaf(v4[kk][e].z, wk[kk], acc[4 * e + 2]);
-                acc[4 * e + 3] = fmaf(v4[kk][e].w, wk[kk], acc[4 * e + 3]);
-              }
-            }
-          }
-        }
-        if (grow < p.Sq) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            *reinterpret_cast<uint4*>(orow + 32 * c + 8 * e) =
-                make_uint4(pack_half2(acc[8 * e] * inv, acc[8 * e + 1] * inv),
-                           pack_half2(acc[8 * e + 2] * inv, acc[8 * e + 3] * inv),
-                           pack_half2(acc[8 * e + 4] * inv, acc[8 * e + 5] * inv),
-                           pack_half2(acc[8 * e + 6] * inv, acc[8 * e + 7] * inv));
-        }
-      }
+      // attn_combine_kernel, launched after this grid, combines the pieces
     }
   }
 
@@ -1859,6 +1767,110 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
   if (warp == 5) {
     tc_fence_after();
     tmem_dealloc2(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------- split-tail combine
+// Combines the partial results of a split schedule, in a grid launched right
+// after the attention kernel on the same stream (programmatic dependent
+// launch: its set-up overlaps the attention kernel's end, griddep_wait holds
+// it until every piece is written). Each (tail unit, query tile or CTA rank,
+// 16-column group) is one CTA of 128 threads, one row per thread, the pieces'
+// loads eight at a time in flight. (In the attention kernels, the last piece
+// to finish combined a unit alone: one 8-GPU rank's shard of C5 at S=32768
+// cuts every unit into ~10 pieces, and that combine -- ~640 KB of L2 reads by
+// one CTA with two pieces in flight -- took ~10-20 us of a 66 us kernel.)
+// Pieces are accumulated in CTA order, so the bits do not depend on which CTA
+// finished first.
+struct CombineParams {
+  const float* ws_o;   // partial O slots, chunk-major [DPC/4][128 rows][4] fp32
+  const float* ws_ml;  // partial (m, l) per slot row
+  __half* o;
+  int Sq, ld, D;       // output rows, row stride, valid columns per slot row
+  int n_qb, unit_rows, tail_unit0, n_tiles, tail_ctas;
+  long long total_steps;
+  int pair;            // 1: D = 512 pair schedule (slot = (cluster, rank, piece))
+};
+
+template <int DPC>
+__global__ void __launch_bounds__(128) attn_combine_kernel(const CombineParams c) {
+  griddep_wait();
+  if (threadIdx.x == 0) griddep_launch_dependents();
+  const int rel = blockIdx.x;  // unit within the split tail
+  const int t = blockIdx.y;    // query tile (D <= 128) or CTA rank (D = 512)
+  const int cg = blockIdx.z;   // 16-column group
+  const int row = threadIdx.x;
+  if (16 * cg >= c.D) return;
+  const int unit = c.tail_unit0 + rel;
+  const int bh = unit / c.n_qb;
+  const int rem = unit - bh * c.n_qb;
+  int grow, col0 = 0;
+  if (c.pair) {
+    grow = ((rem >> 1) * 2 + t) * BM + row;
+    col0 = 256 * (rem & 1);
+  } else {
+    if (t == 1 && c.unit_rows == BM) return;  // single-tile units
+    grow = rem * c.unit_rows + t * BM + row;
+  }
+  if (grow >= c.Sq) return;
+  const long long W = c.total_steps;
+  const int GT = c.tail_ctas;
+  const long long ubase = static_cast<long long>(rel) * c.n_tiles;
+  const int c_lo = owner_cta(ubase, W, GT);
+  const int np = owner_cta(ubase + c.n_tiles - 1, W, GT) - c_lo + 1;
+  // slot row of piece k: range c_lo + k starts inside this unit (its first
+  // tail segment, slot 0) iff floor(c * W / GT) >= ubase, i.e. c * W >= ubase * GT
+  auto piece_row = [&](int k) -> long long {
+    const long long c2 = c_lo + k;
+    const long long which = (c2 * W >= ubase * GT) ? 0 : 1;
+    const long long slot = c.pair ? (c2 * 2 + t) * 2 + which : (c2 * 2 + which) * 2 + t;
+    return slot * BM + row;
+  };
+  auto piece_ml = [&](long long rb) -> float2 { return __ldcg(reinterpret_cast<const float2*>(c.ws_ml + rb * 2)); };
+  float m_all = -INFINITY;
+  for (int k = 0; k < np; ++k) m_all = fmaxf(m_all, piece_ml(piece_row(k)).x);
+  float l_all = 0.f;
+  for (int k = 0; k < np; ++k) {
+    const float2 ml = piece_ml(piece_row(k));
+    l_all = fmaf(ml.y, ex2_approx(ml.x - m_all), l_all);
+  }
+  const float inv = 1.f / l_all;
+  float acc[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+  for (int k0 = 0; k0 < np; k0 += 8) {
+    float4 v[8][4];
+    float w[8];
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int k = (k0 + kk < np) ? k0 + kk : k0;  // a duplicate load, never accumulated
+      const long long rb = piece_row(k);
+      w[kk] = ex2_approx(piece_ml(rb).x - m_all);
+      const long long sl = rb / BM;
+      const float* base = c.ws_o + sl * BM * DPC + (rb - sl * BM) * 4;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[kk][q] = __ldcg(reinterpret_cast<const float4*>(base + (4 * cg + q) * BM * 4));
+    }
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      if (k0 + kk < np) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[4 * q] = fmaf(v[kk][q].x, w[kk], acc[4 * q]);
+          acc[4 * q + 1] = fmaf(v[kk][q].y, w[kk], acc[4 * q + 1]);
+          acc[4 * q + 2] = fmaf(v[kk][q].z, w[kk], acc[4 * q + 2]);
+          acc[4 * q + 3] = fmaf(v[kk][q].w, w[kk], acc[4 * q + 3]);
+        }
+      }
+    }
+  }
+  __half* orow = c.o + (static_cast<long long>(bh) * c.Sq + grow) * c.ld + col0 + 16 * cg;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (16 * cg + 8 * h < c.D)
+      *reinterpret_cast<uint4*>(orow + 8 * h) =
+          make_uint4(pack_half2(acc[8 * h] * inv, acc[8 * h + 1] * inv), pack_half2(acc[8 * h + 2] * inv, acc[8 * h + 3] * inv),
+                     pack_half2(acc[8 * h + 4] * inv, acc[8 * h + 5] * inv), pack_half2(acc[8 * h + 6] * inv, acc[8 * h + 7] * inv));
   }
 }
 
@@ -1994,6 +2006,7 @@ unsigned long long timeout_ns_from_env() {
   return v;
 }
 
+
 // Launch epochs tag the split counters (56 bits: never reused in practice).
 // The sequence starts at a per-process, per-load pseudo-random point (clock,
 // pid and this library's load address through the splitmix64 finaliser), so
@@ -2080,13 +2093,25 @@ bool make_plan(long long BH, int Sq, int Skv, int num_sms, bool allow_split, Pla
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-// Workspace of a split plan: [counters][partial (m, l)][partial O].
+// Workspace of a split plan: [counters][partial (m, l)][partial O], slots of
+// 128 rows per (CTA, piece, query tile), one counter per (tail unit, tile).
 size_t workspace_bytes(const Plan& pl, int DP) {
   if (!pl.split) return 0;
   const size_t slots = static_cast<size_t>(pl.tail_ctas) * 2 * 2 * fa::BM;
   return align256(static_cast<size_t>(pl.n_units - pl.tail_unit0) * 2 * sizeof(unsigned long long)) +
          align256(slots * 2 * sizeof(float)) + slots * DP * sizeof(float);
 }
+
+// Who combines the pieces of a split D <= 128 plan: units cut into few pieces
+// (fewer than 3 CTAs per tail unit on average) are combined in the attention
+// kernel by the piece that finishes last, which overlaps the other CTAs' work
+// (C2: 1145 vs 1075 TFLOP/s with the separate combine); units cut into many
+// are combined by attn_combine_kernel, all of them in parallel (one 8-GPU
+// rank's shard of C5 at S=32768, ~9 pieces per unit: 514 -> 601).
+bool combine_in_kernel(const Plan& pl) {
+  return static_cast<long long>(pl.tail_ctas) < 3ll * (pl.n_units - pl.tail_unit0);
+}
+
 
 // Launches a kernel with programmatic stream serialization: back-to-back
 // calls on one stream then overlap the next call's launch and set-up with the
@@ -2120,6 +2145,28 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, int smem, cudaSt
     e = cudaLaunchKernelEx(&cfg, kernel, args...);
   }
   return (e == cudaSuccess && cudaGetLastError() == cudaSuccess) ? GFX906_B200_OK : GFX906_B200_ECUDA;
+}
+
+// Launches the combine of a split plan after the attention kernel.
+int launch_combine(const Plan& pl, const fa::Params& prm, int dpc, int ld, int dvalid, int pair, cudaStream_t stream) {
+  fa::CombineParams c{};
+  c.ws_o = prm.ws_o;
+  c.ws_ml = prm.ws_ml;
+  c.o = prm.o;
+  c.Sq = prm.Sq;
+  c.ld = ld;
+  c.D = dvalid;
+  c.n_qb = pl.n_qb;
+  c.unit_rows = pl.unit_rows;
+  c.tail_unit0 = pl.tail_unit0;
+  c.n_tiles = pl.n_tiles;
+  c.tail_ctas = pl.tail_ctas;
+  c.total_steps = pl.total_steps;
+  c.pair = pair;
+  const dim3 grid(static_cast<unsigned>(pl.n_units - pl.tail_unit0), 2, static_cast<unsigned>(dpc / 16));
+  if (dpc == 64) return launch_pdl(fa::attn_combine_kernel<64>, grid, dim3(128), 0, stream, 1, c);
+  if (dpc == 128) return launch_pdl(fa::attn_combine_kernel<128>, grid, dim3(128), 0, stream, 1, c);
+  return launch_pdl(fa::attn_combine_kernel<256>, grid, dim3(128), 0, stream, 1, c);
 }
 
 template <int DP>
@@ -2158,9 +2205,12 @@ int launch_dp(const void* q, const void* k, const void* v, void* o, long long BH
     prm.ws_ml = reinterpret_cast<float*>(base);
     base += align256(slots * 2 * sizeof(float));
     prm.ws_o = reinterpret_cast<float*>(base);
+    prm.combine = combine_in_kernel(pl) ? 1 : 0;
   }
-  return launch_pdl(fa::attn_fwd_kernel<DP>, dim3(pl.G), dim3(fa::NUM_THREADS), fa::Cfg<DP>::SMEM_BYTES, stream, 1,
-                    mq, mk, mv, prm);
+  const int rc = launch_pdl(fa::attn_fwd_kernel<DP>, dim3(pl.G), dim3(fa::NUM_THREADS), fa::Cfg<DP>::SMEM_BYTES,
+                            stream, 1, mq, mk, mv, prm);
+  if (rc != GFX906_B200_OK || !pl.split || prm.combine) return rc;
+  return launch_combine(pl, prm, DP, D, D, 0, stream);
 }
 
 template <bool DMAJOR>
@@ -2233,13 +2283,12 @@ bool make_plan512(long long BH, int Sq, int Skv, int num_sms, bool allow_split, 
   return true;
 }
 
-// Workspace of a split D = 512 plan: [counters (unit, rank)][partial (m, l)]
-// [partial O], slots of 128 rows x 256 fp32 per (cluster, rank, piece).
+// Workspace of a split D = 512 plan: [partial (m, l)][partial O], slots of
+// 128 rows x 256 fp32 per (cluster, rank, piece).
 size_t workspace_bytes512(const Plan& pl) {
   if (!pl.split) return 0;
   const size_t slots = static_cast<size_t>(pl.tail_ctas) * 2 * 2 * fa::BM;
-  return align256(static_cast<size_t>(pl.n_units - pl.tail_unit0) * 2 * sizeof(unsigned long long)) +
-         align256(slots * 2 * sizeof(float)) + slots * fa::Cfg512P::DH * sizeof(float);
+  return align256(slots * 2 * sizeof(float)) + slots * fa::Cfg512P::DH * sizeof(float);
 }
 
 // D = 512 (row-major) on CTA pairs: grid x = 2 x clusters, clusters of 2.
@@ -2273,15 +2322,14 @@ int launch_d512_pair(const void* q, const void* k, const void* v, void* o, long 
     if (ws_size < need || (reinterpret_cast<uintptr_t>(ws) & 255u)) return GFX906_B200_EINVAL;
     uint8_t* base = static_cast<uint8_t*>(ws);
     const size_t slots = static_cast<size_t>(pl.tail_ctas) * 2 * 2 * fa::BM;
-    prm.ws_cnt = reinterpret_cast<unsigned long long*>(base);
-    base += align256(static_cast<size_t>(pl.n_units - pl.tail_unit0) * 2 * sizeof(unsigned long long));
-    prm.epoch = next_epoch();
     prm.ws_ml = reinterpret_cast<float*>(base);
     base += align256(slots * 2 * sizeof(float));
     prm.ws_o = reinterpret_cast<float*>(base);
   }
-  return launch_pdl(fa::attn_fwd_d512_pair_kernel, dim3(2 * static_cast<unsigned>(pl.G)), dim3(fa::Cfg512P::THREADS),
-                    fa::Cfg512P::SMEM_BYTES, stream, 2, mq, mk, mv, mo, prm);
+  const int rc = launch_pdl(fa::attn_fwd_d512_pair_kernel, dim3(2 * static_cast<unsigned>(pl.G)),
+                            dim3(fa::Cfg512P::THREADS), fa::Cfg512P::SMEM_BYTES, stream, 2, mq, mk, mv, mo, prm);
+  if (rc != GFX906_B200_OK || !pl.split) return rc;
+  return launch_combine(pl, prm, fa::Cfg512P::DH, 512, fa::Cfg512P::DH, 1, stream);
 }
 
 // Argument checks shared by every entry point. Returns OK and sets *skip when

@@ -67,7 +67,8 @@ GFX906_B200_API size_t gfx906_b200_attn_workspace_size(int B, int H, int Sq, int
  * block) across all SMs (partial results are combined on the GPU). The
  * workspace must be 256-byte aligned and at least
  * gfx906_b200_attn_workspace_size() bytes; its contents on entry do not
- * matter (arrival counters are tagged with a per-launch epoch), so it needs
+ * matter (a call reads only the partial results it wrote itself, and its
+ * arrival counters carry a per-launch tag), so it needs
  * no clearing and may be reused for calls of any size. Calls that share a
  * workspace must not overlap on the GPU (use one stream, or one workspace per
  * stream). Extension of attn_kernel.hip:710-742 (same arguments plus the
