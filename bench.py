@@ -502,7 +502,7 @@ def run_ours(args, rank, world, local):
             else ("attn_fwd_d512_kernel<true>" if dmajor else "attn_fwd_d512_pair_kernel"),
         },
         "clocks": clocks,
-        "gpu_launches": args.steps * _launches_per_call(cfg),
+        "gpu_launches": args.steps * _launches_per_call(cfg, dmajor),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "ms_per_step": e2e_ms / e2e_steps},
@@ -514,8 +514,16 @@ def run_ours(args, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
-def _launches_per_call(cfg: AttnConfig) -> int:
-    return 1
+def _launches_per_call(cfg: AttnConfig, dmajor: bool = False) -> int:
+    """Kernels one call launches: the attention kernel, plus the combine
+    kernel when the plan splits and combines pieces in a second kernel."""
+    if dmajor:
+        return 1
+    from gfx906_b200 import build
+    from gfx906_b200.cabi import CABI
+
+    rc, pl = CABI(build.LIB_PATH).plan(cfg.B, cfg.H, cfg.Sq, cfg.Skv, cfg.D, with_workspace=True)
+    return 2 if rc == 0 and pl["split"] == 2 else 1
 
 
 def _c_launcher(dmajor: bool = False):

@@ -2451,14 +2451,14 @@ int gfx906_b200_attn_plan(int B, int H, int Sq, int Skv, int D, int with_workspa
     // CTAs (2 per cluster); unit_rows = query rows of a unit (a pair of tiles)
     if (!make_plan512(BH, Sq, Skv, num_sms, with_workspace != 0, &pl)) return GFX906_B200_EINVAL;
     out4[0] = 2 * pl.G;
-    out4[1] = pl.split;
+    out4[1] = pl.split ? 2 : 0;  // D = 512 pieces are always combined by attn_combine_kernel
     out4[2] = 2 * pl.tail_ctas;
     out4[3] = pl.unit_rows;
     return GFX906_B200_OK;
   }
   if (!make_plan(BH, Sq, Skv, num_sms, with_workspace != 0, &pl)) return GFX906_B200_EINVAL;
   out4[0] = pl.G;
-  out4[1] = pl.split;
+  out4[1] = pl.split ? (combine_in_kernel(pl) ? 1 : 2) : 0;
   out4[2] = pl.tail_ctas;
   out4[3] = pl.unit_rows;
   return GFX906_B200_OK;

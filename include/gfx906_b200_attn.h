@@ -82,9 +82,10 @@ GFX906_B200_API int gfx906_b200_attn_launch_ws(const void* q, const void* k, con
  * gfx906_b200_attn_launch_ws (with_workspace != 0) picks for these sizes on
  * a GPU with num_sms SMs (num_sms <= 0: the current device, which must then
  * be an sm_100 GPU; num_sms > 0 touches no GPU): out4[0] = CTAs launched,
- * out4[1] = 1 when the key range is split across CTAs, out4[2] = CTAs
- * sharing the split key range, out4[3] = query rows per work unit (128 or
- * 256). All zero when nothing is launched (an empty problem, Skv == 0).
+ * out4[1] = 0 for whole units, 1 when the key range is split across CTAs and
+ * the pieces are combined inside the attention kernel, 2 when they are
+ * combined by a second kernel launched after it, out4[2] = CTAs sharing the
+ * split key range, out4[3] = query rows per work unit (128 or 256). All zero when nothing is launched (an empty problem, Skv == 0).
  * Returns a GFX906_B200_* status. No reference counterpart: the reference's
  * grid is always (B*H, ceil(Sq/64)) (attn_kernel.hip:714-741). */
 GFX906_B200_API int gfx906_b200_attn_plan(int B, int H, int Sq, int Skv, int D,

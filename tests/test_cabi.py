@@ -87,14 +87,18 @@ def test_plan_fills_a_b200_for_small_row_shards(lib):
     """One 8-GPU rank's shard of one long head (C5 at S=32768: 4096 query rows
     x 32768 keys, 16 units of 256 rows x 256 key tiles) gets every SM."""
     pl = plan(lib, 1, 1, 4096, 32768, 64)
-    assert pl["split"] == 1 and pl["ctas"] == B200_SMS and pl["tail_ctas"] == B200_SMS
+    # ~9 CTAs per unit: the pieces are combined by a second kernel
+    assert pl["split"] == 2 and pl["ctas"] == B200_SMS and pl["tail_ctas"] == B200_SMS
     assert pl["unit_rows"] == 256
     # C5 at S=131072 on 8 GPUs (64 units per rank) and on one GPU
     assert plan(lib, 1, 1, 16384, 131072, 64)["ctas"] == B200_SMS
     assert plan(lib, 1, 1, 131072, 131072, 64)["ctas"] == B200_SMS
     # two units: at most 31 CTAs share a unit's key range
     pl = plan(lib, 1, 1, 512, 4096, 64)
-    assert pl["split"] == 1 and pl["ctas"] <= 31 * 2
+    assert pl["split"] == 2 and pl["ctas"] <= 31 * 2
+    # C5 and C5 at S=32768 on one GPU: few pieces per unit, combined in the kernel
+    assert plan(lib, 1, 1, 131072, 131072, 64)["split"] == 1
+    assert plan(lib, 1, 1, 32768, 32768, 64)["split"] == 1
 
 
 def test_plan_short_units(lib):
@@ -112,7 +116,7 @@ def test_plan_short_units(lib):
     # over all 74
     for ws in (True, False):
         assert plan(lib, 1, 4, 4096, 4096, 512, ws=ws) == {"ctas": 148, "split": 0, "tail_ctas": 0, "unit_rows": 256}
-    assert plan(lib, 1, 4, 512, 4096, 512) == {"ctas": 148, "split": 1, "tail_ctas": 148, "unit_rows": 256}
+    assert plan(lib, 1, 4, 512, 4096, 512) == {"ctas": 148, "split": 2, "tail_ctas": 148, "unit_rows": 256}
     assert plan(lib, 1, 4, 512, 4096, 512, ws=False)["ctas"] == 32
     # 4 units of one key tile: whole units, one cluster each
     assert plan(lib, 1, 1, 256, 100, 512) == {"ctas": 4, "split": 0, "tail_ctas": 0, "unit_rows": 256}
