@@ -67,6 +67,9 @@ def parse_args():
     ap.add_argument("--strong-steps", type=int, default=10,
                     help="steps of each leg of the strong-scaling record (C5, C5s rows-sharded)")
     ap.add_argument("--no-strong", action="store_true", help="skip the strong-scaling record")
+    ap.add_argument("--strong-reps", type=int, default=2, help="interleaved repeats of the strong legs (best kept)")
+    ap.add_argument("--reserve-sms", type=int, default=8,
+                    help="SMs the pipelined strong leg leaves to the NCCL kernels (the attention kernel takes the rest)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--layout", default="rows", choices=["rows", "dmajor"],
@@ -255,14 +258,17 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, warmup: int) -> dict:
+def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, warmup: int,
+                reserve_sms: int = 8, reps: int = 2) -> dict:
     """Strong scaling of one problem: cfg's query rows cut over the ranks in
     whole 256-row blocks, K and V broadcast from rank 0 with NCCL, O gathered
     with all_gather_into_tensor (gfx906_b200.shard.attention_by_rows). Times,
     each the max over ranks of CUDA events on the launching stream: the kernel
-    alone, the broadcast alone, the gather alone, the three in sequence, and
-    the three pipelined across calls (the next call's K/V broadcast overlapping
-    this call's kernel, gathers asynchronous)."""
+    alone, the kernel alone on all SMs but `reserve_sms`, the broadcast alone,
+    the gather alone, the three in sequence, and the three pipelined across
+    calls (shard.attention_by_rows_pipelined: the next call's K/V broadcast
+    and this call's gather run beside the next kernel on the reserved SMs).
+    The legs run interleaved `reps` times; each figure is the best repeat."""
     import gfx906_b200
     from gfx906_b200 import shard
 
@@ -287,28 +293,25 @@ def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, 
             shard._gather_dim(local_out, counts, 2, None, out=out_full)
 
     # pipelined: every call still broadcasts its K/V, runs the kernel and
-    # gathers its O, but the next call's broadcast (other buffers) runs on the
-    # collective stream while this call's kernel runs, and the gathers are
-    # asynchronous
+    # gathers its O, but the next call's broadcast (other buffers) and this
+    # call's gather run on the collective stream beside the next kernel
     kbuf, vbuf = [kd, kd.clone()], [vd, vd.clone()]
     obuf = [out_full, torch.empty_like(out_full)]
 
     def pipelined(n):
-        pending = shard.broadcast_kv(kbuf[0], vbuf[0], src=0, async_op=True)
-        gathers = []
-        for i in range(n):
-            for w in pending:
-                w.wait()
-            if i + 1 < n:
-                pending = shard.broadcast_kv(kbuf[(i + 1) % 2], vbuf[(i + 1) % 2], src=0, async_op=True)
-            local = gfx906_b200.attn(q_rows, kbuf[i % 2], vbuf[i % 2], cfg.scale)
-            gathers.append(shard.gather_rows(local, cfg.Sq, obuf[i % 2], async_op=True))
-        for w in gathers:
-            if w is not None:
-                w.wait()
+        calls = [(q_rows, kbuf[i % 2], vbuf[i % 2], cfg.scale, obuf[i % 2]) for i in range(n)]
+        shard.attention_by_rows_pipelined(calls, cfg.Sq, src=0, reserve_sms=reserve_sms)
+
+    n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
+
+    def kernel_reserved(n):
+        with gfx906_b200.sm_limit(max(2, n_sms - reserve_sms)):
+            for _ in range(n):
+                gfx906_b200.attn(q_rows, kd, vd, cfg.scale)
 
     legs = {
         "kernel": (lambda n: [gfx906_b200.attn(q_rows, kd, vd, cfg.scale) for _ in range(n)]),
+        "kernel_reserved": kernel_reserved,
         "broadcast": (lambda n: [bcast() for _ in range(n)]),
         "gather": (lambda n: [gather() for _ in range(n)]),
         "with_collectives": (lambda n: [shard.attention_by_rows(q_rows, kd, vd, cfg.scale, cfg.Sq, src=0,
@@ -316,24 +319,31 @@ def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, 
         "pipelined": pipelined,
     }
     ms = {}
-    for name, fn in legs.items():  # every rank runs the same legs in the same order
-        fn(max(3, warmup))  # NCCL's lazy set-up stays out of the timing
-        torch.cuda.synchronize()
-        barrier(world)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        fn(steps)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-        ms[name] = max_over_ranks(e0.elapsed_time(e1), world) / steps
+    for rep in range(reps):  # legs interleaved, best of `reps` (each the max over ranks)
+        for name, fn in legs.items():  # every rank runs the same legs in the same order
+            if rep == 0:
+                fn(max(3, warmup))  # NCCL's lazy set-up stays out of the timing
+            torch.cuda.synchronize()
+            barrier(world)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            # ~0.5 ms of GPU spin ahead of the start event: the host queues the
+            # first calls meanwhile, so its launch latency stays out of the timing
+            torch.cuda._sleep(1 << 20)
+            e0.record(stream)
+            fn(steps)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            barrier(world)
+            t = max_over_ranks(e0.elapsed_time(e1), world) / steps
+            ms[name] = min(ms.get(name, t), t)
     kv_bytes = 2 * kd.numel() * kd.element_size()
     o_bytes = out_full.numel() * out_full.element_size()
     return {
         "workload": f"{cfg.name}: {cfg.describe()}",
-        "ranks": world, "rows_per_rank": sh.size, "steps": steps,
-        "kernel_ms": ms["kernel"], "broadcast_ms": ms["broadcast"], "gather_ms": ms["gather"],
+        "ranks": world, "rows_per_rank": sh.size, "steps": steps, "repeats": reps,
+        "kernel_ms": ms["kernel"], "kernel_reserved_ms": ms["kernel_reserved"], "reserve_sms": reserve_sms,
+        "broadcast_ms": ms["broadcast"], "gather_ms": ms["gather"],
         "with_collectives_ms": ms["with_collectives"], "pipelined_ms": ms["pipelined"],
         "value_kernel": cfg.flops / (ms["kernel"] * 1e-3) / 1e12,
         "value_with_collectives": cfg.flops / (ms["with_collectives"] * 1e-3) / 1e12,
@@ -355,7 +365,7 @@ def run_rows(args, rank, world, local):
     cfg = CONFIGS[args.config]
     sampler = ClockSampler(local)
     with sampler:
-        rec = strong_rows(cfg, rank, world, local, args.steps, args.warmup)
+        rec = strong_rows(cfg, rank, world, local, args.steps, args.warmup, args.reserve_sms, args.strong_reps)
     if rank != 0:
         return
     line = {
@@ -473,7 +483,8 @@ def run_ours(args, rank, world, local):
     strong = []
     if not args.no_strong:
         for name in ("C5", "C5s"):
-            strong.append(strong_rows(CONFIGS[name], rank, world, local, args.strong_steps, 3))
+            strong.append(strong_rows(CONFIGS[name], rank, world, local, args.strong_steps, 3, args.reserve_sms,
+                                      args.strong_reps))
 
     if rank != 0:
         return

@@ -11,11 +11,17 @@ Public entry points:
 * ``attn_host(q, k, v, scale)``: the same operator for q, k, v in (pinned)
   host memory, uploads and downloads overlapped with the kernel per block of
   (batch x head) units (``host.py``).
+* ``set_sm_limit(n)`` / ``sm_limit(n)``: cap the SMs the persistent kernels
+  use, leaving the rest to kernels of other streams (NCCL collectives of a
+  sharded pipeline, ``shard.attention_by_rows_pipelined``).
 """
+
+import contextlib
 
 from .gfx906_attn import is_sm100, last_error, load_attention
 
-__all__ = ["attn", "attn_dmajor", "attn_host", "device_status", "is_sm100", "load_attention", "last_error"]
+__all__ = ["attn", "attn_dmajor", "attn_host", "device_status", "is_sm100", "load_attention", "last_error",
+           "set_sm_limit", "sm_limit"]
 
 
 def _module_or_raise():
@@ -47,3 +53,20 @@ def attn_host(q, k, v, scale, out=None, device=None, blocks=None, non_blocking=F
     from .host import attn_host as _attn_host
 
     return _attn_host(q, k, v, scale, out=out, device=device, blocks=blocks, non_blocking=non_blocking)
+
+
+def set_sm_limit(sms: int) -> int:
+    """Caps, process-wide, the SMs the persistent kernels plan for (0: all of
+    the device's); returns the previous cap. D = 512 uses sms // 2 two-CTA
+    clusters (at least one)."""
+    return int(_module_or_raise().set_sm_limit(int(sms)))
+
+
+@contextlib.contextmanager
+def sm_limit(sms: int):
+    """``set_sm_limit(sms)`` for the duration of a ``with`` block."""
+    prev = set_sm_limit(sms)
+    try:
+        yield
+    finally:
+        set_sm_limit(prev)

@@ -47,6 +47,7 @@ class CABI:
         d.gfx906_b200_attn_noalloc_capacity.restype = ctypes.c_size_t
         d.gfx906_b200_attn_plan.argtypes = [_c_int] * 7 + [ctypes.POINTER(_c_int)]
         d.gfx906_b200_attn_plan.restype = _c_int
+        d.gfx906_b200_attn_set_sm_limit.argtypes, d.gfx906_b200_attn_set_sm_limit.restype = [_c_int], _c_int
         d.gfx906_b200_attn_flops.argtypes = [_c_int] * 5
         d.gfx906_b200_attn_flops.restype = ctypes.c_double
 
@@ -72,6 +73,10 @@ class CABI:
         buf = (_c_int * 4)()
         rc = self.dll.gfx906_b200_attn_plan(B, H, Sq, Skv, D, 1 if with_workspace else 0, num_sms, buf)
         return rc, dict(zip(("ctas", "split", "tail_ctas", "unit_rows"), list(buf)))
+
+    def set_sm_limit(self, sms: int) -> int:
+        """Caps the SMs the persistent kernels use (0: all); returns the previous cap."""
+        return self.dll.gfx906_b200_attn_set_sm_limit(sms)
 
     def last_error(self) -> int:
         return self.dll.gfx906_b200_attn_last_error()

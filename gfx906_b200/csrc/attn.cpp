@@ -138,9 +138,17 @@ torch::Tensor attn_dmajor(torch::Tensor q, torch::Tensor k, torch::Tensor v, dou
 // Returns 0 when no kernel wait has timed out. Synchronises.
 int64_t device_status(bool reset) { return gfx906_b200_attn_device_status(reset ? 1 : 0); }
 
+// Process-wide cap on the SMs the persistent kernels use (0 = all); returns
+// the previous cap (see gfx906_b200_attn_set_sm_limit).
+int64_t set_sm_limit(int64_t sms) {
+  TORCH_CHECK(sms >= 0 && sms <= INT32_MAX, "kernel: sm limit must be >= 0");
+  return gfx906_b200_attn_set_sm_limit(static_cast<int>(sms));
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn", &attn, "flash-attention forward (fp16 [B,H,S,D], sm_100a)");
   m.def("attn_out", &attn_out, "flash-attention forward into a given contiguous fp16 output tensor");
   m.def("attn_dmajor", &attn_dmajor, "flash-attention forward on transposed [B,H,D,S] fp16, D = 512");
   m.def("device_status", &device_status, "device status word (0 = ok)", pybind11::arg("reset") = false);
+  m.def("set_sm_limit", &set_sm_limit, "cap on the SMs the persistent kernels use (0 = all); returns the previous");
 }

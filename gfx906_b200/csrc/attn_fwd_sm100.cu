@@ -1994,7 +1994,18 @@ int check_device(int* dev_out) {
   return GFX906_B200_OK;
 }
 
-int device_sms(int dev) { return g_dev[dev].num_sms > 0 ? g_dev[dev].num_sms : 1; }
+// Upper bound on the SMs a launch plans for (0: all of the device's), set by
+// gfx906_b200_attn_set_sm_limit. A persistent grid of fewer CTAs than SMs
+// leaves the rest to kernels on other streams, e.g. the NCCL collectives of
+// the next or previous call of a sharded pipeline, which otherwise cannot
+// start until the attention kernel ends.
+std::atomic<int> g_sm_limit{0};
+
+int device_sms(int dev) {
+  const int n = g_dev[dev].num_sms > 0 ? g_dev[dev].num_sms : 1;
+  const int lim = g_sm_limit.load(std::memory_order_relaxed);
+  return (lim > 0 && lim < n) ? lim : n;
+}
 
 unsigned long long timeout_ns_from_env() {
   static unsigned long long v = [] {
@@ -2483,6 +2494,8 @@ void launch(const void* q, const void* k, const void* v, void* o, int B, int H, 
 }
 
 int gfx906_b200_attn_last_error(void) { return t_last_error; }
+
+int gfx906_b200_attn_set_sm_limit(int sms) { return g_sm_limit.exchange(sms > 0 ? sms : 0); }
 
 const char* gfx906_b200_attn_error_string(int status) {
   switch (status) {

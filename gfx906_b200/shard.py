@@ -199,6 +199,59 @@ def gather_rows(local, Sq: int, out: torch.Tensor, group=None, async_op: bool = 
     return None
 
 
+def _device_sms(t: torch.Tensor) -> int:
+    return torch.cuda.get_device_properties(t.device).multi_processor_count
+
+
+def attention_by_rows_pipelined(calls, Sq: int, src: int = 0, group=None, reserve_sms: int = 8,
+                                local_attn: Optional[Callable] = None):
+    """A sequence of query-row sharded calls with their collectives overlapped.
+
+    calls: iterable of (q_rows, k, v, scale, out) as for attention_by_rows
+    (k, v full on rank `src`, receive buffers elsewhere; out the gathered
+    [B, H, Sq, D] output). Call i + 1's K/V broadcast and call i's output
+    gather run on the collective stream while call i's kernel runs, so
+    consecutive calls must not share k, v or out buffers (alternating two
+    sets is enough: a broadcast into a set is enqueued after the kernel that
+    last read it). The kernel is capped at the device's SMs minus
+    `reserve_sms`, which the NCCL kernels use meanwhile (a persistent kernel
+    on every SM would hold them off until it ends). Returns the outputs, all
+    written once the current stream reaches this point.
+    """
+    import contextlib
+
+    calls = list(calls)
+    if not calls:
+        return []
+    attn = local_attn or _default_attn()
+    world, rank = _group_world(group)
+    sh = row_shard(Sq, rank, world)
+    limit = contextlib.nullcontext()
+    if local_attn is None and reserve_sms > 0 and calls[0][0].is_cuda:
+        import gfx906_b200
+
+        limit = gfx906_b200.sm_limit(max(2, _device_sms(calls[0][0]) - reserve_sms))
+    outs = []
+    with limit:
+        pending = broadcast_kv(calls[0][1], calls[0][2], src=src, group=group, async_op=True)
+        gathers = []
+        for i, (q_rows, k, v, scale, out) in enumerate(calls):
+            if q_rows.shape[2] != sh.size:
+                raise ValueError(f"rank {rank} holds {q_rows.shape[2]} query rows, its shard is {sh.size}")
+            for w in pending:
+                w.wait()
+            pending = []
+            if i + 1 < len(calls):
+                pending = broadcast_kv(calls[i + 1][1], calls[i + 1][2], src=src, group=group, async_op=True)
+            local = attn(q_rows, k, v, scale) if sh.size > 0 else q_rows.new_zeros(q_rows.shape)
+            gathers.append(gather_rows(local, Sq, out, group=group, async_op=True))
+            outs.append(out)
+        for w in gathers:
+            if w is not None:
+                w.wait()
+    return outs
+
+
 def choose_partition(B: int, H: int, world: int) -> str:
     """"heads" while every rank gets at least one (batch x head) unit, else "rows"."""
     return "heads" if B * H >= world else "rows"

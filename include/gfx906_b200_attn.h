@@ -91,6 +91,18 @@ GFX906_B200_API int gfx906_b200_attn_launch_ws(const void* q, const void* k, con
 GFX906_B200_API int gfx906_b200_attn_plan(int B, int H, int Sq, int Skv, int D,
                           int with_workspace, int num_sms, int* out4);
 
+/* Caps the SMs the persistent kernels plan for, process-wide: launches after
+ * this call use at most `sms` CTAs (D = 512: sms / 2 two-CTA clusters, at
+ * least one), and gfx906_b200_attn_workspace_size and
+ * gfx906_b200_attn_plan(num_sms = 0) follow the cap. sms <= 0 removes it.
+ * Returns the previous cap (0 = none). The SMs left over run kernels of
+ * other streams beside the attention kernel -- the NCCL broadcast of the
+ * next call's K/V and the gather of the previous call's output in a sharded
+ * pipeline -- which otherwise wait until the all-SM kernel ends. Set it
+ * while no other thread is between workspace_size and launch_ws. No
+ * reference counterpart (the reference has no persistent grid). */
+GFX906_B200_API int gfx906_b200_attn_set_sm_limit(int sms);
+
 /* Allocation-free form of gfx906_b200_attn_launch_ws, for callers that cannot
  * allocate device memory (a plugin whose host runtime owns all device memory,
  * an application with a fixed memory budget, a latency-critical path where

@@ -134,3 +134,11 @@ def test_noalloc_records_argument_errors(lib):
     assert lib.last_error() == STATUS["EHEADDIM"]
     assert lib.launch_noalloc_status(None, None, None, None, 0, 1, 8, 8, 64, 0.1) == STATUS["OK"]
     assert lib.last_error() == STATUS["OK"]
+
+
+def test_sm_limit_round_trip(lib):
+    """The SM cap is process-wide state: set returns the previous value and
+    values <= 0 mean no cap (no GPU needed to set it)."""
+    assert lib.set_sm_limit(100) == 0
+    assert lib.set_sm_limit(-5) == 100
+    assert lib.set_sm_limit(0) == 0

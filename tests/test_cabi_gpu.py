@@ -155,3 +155,25 @@ def test_workspace_shared_between_library_instances(lib, tmp_path):
     check_rows(outs[0], q, k, v, D ** -0.5, sample_rows(Sq, n_each=32, seed=8), what="two library instances")
     assert lib.device_status(reset=False) == STATUS["OK"]
     assert lib2.device_status(reset=False) == STATUS["OK"]
+
+
+@pytest.mark.parametrize("limit", [140, 137])
+def test_sm_limit_caps_the_grid(lib, limit):
+    """With the SMs capped (as a sharded pipeline does to leave SMs to NCCL)
+    every schedule plans at most `limit` CTAs (D = 512: limit // 2 clusters)
+    and still matches the oracle, workspace sized for the capped plan."""
+    shapes = [(1, 1, 4096, 32768, 64), (1, 24, 4096, 4096, 128), (1, 4, 512, 4096, 512), (1, 4, 4096, 4096, 512)]
+    prev = lib.set_sm_limit(limit)
+    try:
+        for shape in shapes:
+            B, H, Sq, Skv, D = shape
+            rc, pl = lib.plan(B, H, Sq, Skv, D, with_workspace=True)
+            assert rc == STATUS["OK"]
+            assert pl["ctas"] <= (limit if D != 512 else 2 * (limit // 2)), (shape, pl)
+            q, k, v = make_qkv(B, H, Sq, Skv, D, seed=limit + D)
+            out = run(lib, q, k, v, D ** -0.5, True, {})
+            check_rows(out, q, k, v, D ** -0.5, sample_rows(Sq, n_each=32, seed=D), what=f"{shape} limit={limit}")
+    finally:
+        assert lib.set_sm_limit(prev) == limit
+    rc, pl = lib.plan(1, 24, 4096, 4096, 128, with_workspace=True)
+    assert pl["ctas"] == torch.cuda.get_device_properties(0).multi_processor_count

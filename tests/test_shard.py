@@ -81,36 +81,25 @@ def _worker(rank, world, port, mode, result_q):
 
 
 def _pipelined(rank, world, result_q):
-    """Three calls with the next call's K/V broadcast while this one computes,
-    and each output gathered asynchronously; every output must equal the
-    unsharded result of its own inputs."""
+    """Three calls through attention_by_rows_pipelined (the next call's K/V
+    broadcast while this one computes, each output gathered asynchronously):
+    every output must equal the unsharded result of its own inputs."""
     Sq, Skv, D = 256 * world * 2, 300, 64
     scale = D ** -0.5
     inputs = [make_qkv(1, 1, Sq, Skv, D, seed=20 + i) for i in range(3)]
     sh = shard.row_shard(Sq, rank, world)
+    # receive buffers alternate between two sets on the ranks that receive
     kbuf = [torch.zeros(1, 1, Skv, D, dtype=torch.float16) for _ in range(2)]
     vbuf = [torch.zeros(1, 1, Skv, D, dtype=torch.float16) for _ in range(2)]
     outs = [torch.full((1, 1, Sq, D), float("nan"), dtype=torch.float16) for _ in range(3)]
-
-    def load(i):
-        if rank == 0:
-            kbuf[i % 2].copy_(inputs[i][1])
-            vbuf[i % 2].copy_(inputs[i][2])
-        return shard.broadcast_kv(kbuf[i % 2], vbuf[i % 2], src=0, async_op=True)
-
-    pending = load(0)
-    gathers = []
+    calls = []
     for i in range(3):
-        for w in pending:
-            w.wait()
-        if i + 1 < 3:
-            pending = load(i + 1)
-        q_rows = inputs[i][0][:, :, sh.start:sh.stop].contiguous()
-        local = oracle_attn(q_rows, kbuf[i % 2].clone(), vbuf[i % 2].clone(), scale)
-        gathers.append(shard.gather_rows(local, Sq, outs[i], async_op=True))
-    for w in gathers:
-        if w is not None:
-            w.wait()
+        q, k, v = inputs[i]
+        if rank != 0:
+            k, v = kbuf[i % 2], vbuf[i % 2]
+        calls.append((q[:, :, sh.start:sh.stop].contiguous(), k, v, scale, outs[i]))
+    got = shard.attention_by_rows_pipelined(calls, Sq, src=0, local_attn=oracle_attn)
+    assert all(a is b for a, b in zip(got, outs))
     if rank == 0:
         err = 0.0
         for i in range(3):

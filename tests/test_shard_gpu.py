@@ -56,6 +56,26 @@ def _worker(rank, world, port, result_q):
         out = shard.attention_sharded(q.cuda(), k.cuda(), v.cuda(), 512 ** -0.5)
         full = gfx906_b200.attn(q.cuda(), k.cuda(), v.cuda(), 512 ** -0.5)
         errs.append(float((out.float() - full.float()).abs().max()))
+        # pipelined: 3 calls, K/V of the next broadcast and O gathered beside
+        # the kernel, which leaves 8 SMs to NCCL (a different split, so the
+        # tolerance, not identical bits)
+        Sq, Skv, D = 2048 * world, 4096, 64
+        ins = [make_qkv(1, 1, Sq, Skv, D, seed=30 + i) for i in range(3)]
+        sh = shard.row_shard(Sq, rank, world)
+        kb = [torch.zeros(1, 1, Skv, D, dtype=torch.float16, device="cuda") for _ in range(2)]
+        vb = [torch.zeros(1, 1, Skv, D, dtype=torch.float16, device="cuda") for _ in range(2)]
+        calls = []
+        for i, (q, k, v) in enumerate(ins):
+            if rank == 0:
+                kd, vd = k.cuda(), v.cuda()
+            else:
+                kd, vd = kb[i % 2], vb[i % 2]
+            out = torch.full((1, 1, Sq, D), float("nan"), dtype=torch.float16, device="cuda")
+            calls.append((q[:, :, sh.start:sh.stop].contiguous().cuda(), kd, vd, D ** -0.5, out))
+        outs = shard.attention_by_rows_pipelined(calls, Sq, src=0, reserve_sms=8)
+        for (q, k, v), out in zip(ins, outs):
+            full = gfx906_b200.attn(q.cuda(), k.cuda(), v.cuda(), D ** -0.5)
+            errs.append(float((out.float() - full.float()).abs().max()))
         torch.cuda.synchronize()
         if rank == 0:
             result_q.put(errs)
@@ -72,4 +92,4 @@ def test_sharded_attention_nccl():
     q = ctx.Queue()
     mp.start_processes(_worker, args=(world, _free_port(), q), nprocs=world, start_method="spawn", join=True)
     errs = q.get(timeout=120)
-    assert all(e <= 2e-3 for e in errs) and len(errs) == 3, errs
+    assert all(e <= 2e-3 for e in errs) and len(errs) == 6, errs
