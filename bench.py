@@ -68,7 +68,7 @@ def parse_args():
                     help="steps of each leg of the strong-scaling record (C5, C5s rows-sharded)")
     ap.add_argument("--no-strong", action="store_true", help="skip the strong-scaling record")
     ap.add_argument("--strong-reps", type=int, default=2, help="interleaved repeats of the strong legs (best kept)")
-    ap.add_argument("--reserve-sms", type=int, default=8,
+    ap.add_argument("--reserve-sms", type=int, default=16,
                     help="SMs the pipelined strong leg leaves to the NCCL kernels (the attention kernel takes the rest)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -259,7 +259,7 @@ def run_reference(args, rank, world):
 
 
 def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, warmup: int,
-                reserve_sms: int = 8, reps: int = 2) -> dict:
+                reserve_sms: int = 16, reps: int = 2) -> dict:
     """Strong scaling of one problem: cfg's query rows cut over the ranks in
     whole 256-row blocks, K and V broadcast from rank 0 with NCCL, O gathered
     with all_gather_into_tensor (gfx906_b200.shard.attention_by_rows). Times,
