@@ -489,7 +489,7 @@ def run_ours(args, rank, world, local):
     if rank != 0:
         return
     peak_tf, _, peak_kind = load_peaks()
-    traffic = None if dmajor else profiled_traffic(base.name)
+    traffic = profiled_traffic(base.name + ("_dmajor" if dmajor else ""))
     clocks = sampler.summary()
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -510,7 +510,7 @@ def run_ours(args, rank, world, local):
             "traffic": traffic,
             "algorithmic_bytes": cfg.io_bytes,
             "kernel": f"attn_fwd_kernel<{128 if cfg.D == 128 else 64}>" if cfg.D <= 128
-            else ("attn_fwd_d512_kernel<true>" if dmajor else "attn_fwd_d512_pair_kernel"),
+            else f"attn_fwd_d512_pair_kernel<{'true' if dmajor else 'false'}>",
         },
         "clocks": clocks,
         "gpu_launches": args.steps * _launches_per_call(cfg, dmajor),

@@ -995,352 +995,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
-// ----------------------------------------------------------------- D = 512
-// Head dim 512 (the reference's VAE mid-block path, attn_kernel.hip:525-708).
-// An fp32 O tile of 128 rows x 512 columns fills all of TMEM, so a CTA owns
-// one 128-row query tile and one half (256 columns) of the head dim: blockIdx.x
-// = 2 * query tile + half. Both halves compute the full S = Q K^T (K = 512):
-// 1.5x the minimum tensor work, in exchange for no inter-CTA traffic.
-// Q stays resident (128 KiB); K and the V half stream through a ring of three
-// 32 KiB slots, each slot a [128 keys x 128 head-dim] tile (two swizzled 64-col
-// boxes): per key tile K0..K3 (head dims 0..511) then, one tile later, V0 V1
-// (this half's 256 head dims). TMEM: S double-buffered at [0,128) / [128,256),
-// O half at [256,512); P of tile j is written over the first 64 columns of
-// its S buffer. MMA order: S(0), S(1), PV(0), S(2), PV(1), ... so the tensor
-// core computes S(j+1) while the softmax warpgroup works on S(j).
-//
-// DMAJOR: every (b, h) matrix is stored transposed, [D][S] with the sequence
-// contiguous -- a [b, c, h, w] feature map is exactly this with H = 1, D = c,
-// S = h * w -- and the kernel reads and writes that layout directly: Q and K
-// become MN-major MMA operands (64 sequence positions per 128-byte row, head
-// dims down the rows), V a K-major one, and O is staged as [256 d][128 rows]
-// and written with one unswizzled TMA store. Nothing is transposed in memory.
-struct Cfg512 {
-  static constexpr int SLOTS = 3;
-  static constexpr int SLOT_BYTES = 2 * CHUNK_BYTES;
-  static constexpr int Q_BYTES = 8 * CHUNK_BYTES;
-  static constexpr int DATA_BYTES = Q_BYTES + SLOTS * SLOT_BYTES;
-  // Q, KV_FULL[3], KV_EMPTY[3], S_FULL[2], P_FULL[2], PV_DONE, O_FULL, DRAIN, EPI
-  static constexpr int B_Q = 0, B_KV_FULL = 1, B_KV_EMPTY = 1 + SLOTS, B_S_FULL = 1 + 2 * SLOTS;
-  static constexpr int B_P_FULL = B_S_FULL + 2, B_PV_DONE = B_P_FULL + 2, B_O_FULL = B_PV_DONE + 1;
-  static constexpr int B_DRAIN = B_O_FULL + 1, B_EPI = B_DRAIN + 1, NUM_BARS = B_EPI + 1;
-  static constexpr int SMEM_BYTES = 1024 + DATA_BYTES + NUM_BARS * 8 + 16;
-  static constexpr int THREADS = 256;  // softmax warpgroup + control warpgroup
-};
-
-template <bool DMAJOR>
-__global__ void __launch_bounds__(Cfg512::THREADS, 1)
-    attn_fwd_d512_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                         const Params p) {
-  using C = Cfg512;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t s0 = (raw + 1023u) & ~1023u;
-  uint8_t* smem = smem_raw + (s0 - raw);
-  const uint32_t sQ = s0;
-  const uint32_t sRing = s0 + C::Q_BYTES;
-  const uint32_t bars = s0 + C::DATA_BYTES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::DATA_BYTES + C::NUM_BARS * 8);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* drain_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
-
-  const int warp = threadIdx.x / 32;
-  const int lane = threadIdx.x % 32;
-  const int bh = blockIdx.y + p.bh_offset;
-  const int half = blockIdx.x & 1;
-  const int q_row0 = (blockIdx.x >> 1) * BM;
-  const int n_tiles = (p.Skv + BN - 1) / BN;
-  const unsigned long long tmo = p.timeout_ns;
-
-  if (threadIdx.x == 0) {
-    mbar_init(bars + 8 * C::B_Q, 1);
-    for (int s = 0; s < C::SLOTS; ++s) {
-      mbar_init(bars + 8 * (C::B_KV_FULL + s), 1);
-      mbar_init(bars + 8 * (C::B_KV_EMPTY + s), 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bars + 8 * (C::B_S_FULL + i), 1);
-      mbar_init(bars + 8 * (C::B_P_FULL + i), BM);
-    }
-    mbar_init(bars + 8 * C::B_PV_DONE, 1);
-    mbar_init(bars + 8 * C::B_O_FULL, 1);
-    mbar_init(bars + 8 * C::B_DRAIN, 1);
-    mbar_init(bars + 8 * C::B_EPI, BM);
-    *abort_flag = 0;
-    *drain_flag = 0;
-    fence_barrier_init();
-    fence_proxy_async_smem();
-  }
-  if (warp == 5) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  griddep_wait();  // the previous kernel on the stream is complete (see attn_fwd_kernel)
-  if (threadIdx.x == 0) griddep_launch_dependents();
-
-  if (warp == 4) {
-    // ------------------------------------------------------------ producer
-    // Whole-warp loop; one elected lane issues each TMA and expect-tx.
-    {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      tma_prefetch_desc(&tm_o);
-      mbar_arrive_expect_tx_warp(bars + 8 * C::B_Q, C::Q_BYTES);
-      if (DMAJOR) {
-        // [64 rows x 256 d] boxes: M-block mb (rows 64 mb ..) at 64 KiB * mb, d rows of 128 B
-        for (int mb = 0; mb < 2; ++mb)
-          for (int dd = 0; dd < 2; ++dd)
-            tma_load_3d_warp(sQ + mb * 65536 + dd * 32768, &tm_q, bars + 8 * C::B_Q, q_row0 + 64 * mb, 256 * dd, bh);
-      } else {
-        for (int c = 0; c < 8; ++c) tma_load_3d_warp(sQ + c * CHUNK_BYTES, &tm_q, bars + 8 * C::B_Q, c * 64, q_row0, bh);
-      }
-      int it = 0;
-      bool ok = true;
-      // slot order: K(0); then K(j), V(j-1) for j >= 1; then V(n-1)
-      auto load_slot = [&](const CUtensorMap* m, int key0, int d0) -> bool {
-        const int slot = it % C::SLOTS;
-        const uint32_t ph = (it / C::SLOTS) & 1;
-        if (!bwait_warp(bars, C::B_KV_EMPTY + slot, ph ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) return false;
-        const uint32_t full = bars + 8 * (C::B_KV_FULL + slot);
-        mbar_arrive_expect_tx_warp(full, C::SLOT_BYTES);
-        if (DMAJOR) {  // [64 keys x 128 d] boxes, keys 0-63 then 64-127
-          tma_load_3d_warp(sRing + slot * C::SLOT_BYTES, m, full, key0, d0, bh);
-          tma_load_3d_warp(sRing + slot * C::SLOT_BYTES + CHUNK_BYTES, m, full, key0 + 64, d0, bh);
-        } else {       // [128 keys x 64 d] boxes, d0 .. d0+63 then d0+64 ..
-          tma_load_3d_warp(sRing + slot * C::SLOT_BYTES, m, full, d0, key0, bh);
-          tma_load_3d_warp(sRing + slot * C::SLOT_BYTES + CHUNK_BYTES, m, full, d0 + 64, key0, bh);
-        }
-        ++it;
-        return true;
-      };
-      for (int j = 0; j <= n_tiles && ok; ++j) {
-        if (j < n_tiles)
-          for (int s = 0; s < 4 && ok; ++s) ok = load_slot(&tm_k, j * BN, 128 * s);
-        if (j > 0)
-          for (int s = 0; s < 2 && ok; ++s) ok = load_slot(&tm_v, (j - 1) * BN, 256 * half + 128 * s);
-      }
-      if (!ok) {
-        if (!mbar_try_wait(bars + 8 * C::B_Q, 0))
-          wait_slow(bars + 8 * C::B_Q, 0, drain_flag, 100000000ull, C::B_Q, ROLE_PRODUCER);
-        const int first = it > C::SLOTS ? it - C::SLOTS : 0;
-        for (int t = first; t < it; ++t) {
-          const int slot = t % C::SLOTS;
-          const uint32_t ph = (t / C::SLOTS) & 1;
-          if (!mbar_try_wait(bars + 8 * (C::B_KV_FULL + slot), ph))
-            wait_slow(bars + 8 * (C::B_KV_FULL + slot), ph, drain_flag, 100000000ull, C::B_KV_FULL + slot,
-                      ROLE_PRODUCER);
-        }
-      }
-    }
-    __syncwarp();
-  } else if (warp == 5) {
-    // ----------------------------------------------------------- MMA issuer
-    // Whole-warp issue loop; one elected lane issues each group of four MMAs
-    // and each commit.
-    {
-      // Row-major: Q and K K-major, V MN-major. DMAJOR: Q and K MN-major (the
-      // leading byte offset steps to the second 64-wide M / N block), V K-major.
-      constexpr uint32_t IDESC_QK = idesc_f16_f32(BM, BN, DMAJOR ? 1 : 0, DMAJOR ? 1 : 0);
-      constexpr uint32_t IDESC_PV = idesc_f16_f32(BM, 128, 0, DMAJOR ? 0 : 1);
-      const uint64_t dQ = sdesc_sw128(sQ, DMAJOR ? 65536 : 16, 1024);
-      const uint64_t dK = sdesc_sw128(sRing, DMAJOR ? CHUNK_BYTES : 16, 1024);
-      const uint64_t dV = sdesc_sw128(sRing, DMAJOR ? 16 : CHUNK_BYTES, 1024);
-      const uint32_t tO = tmem + 256;
-      int it = 0;
-      bool ok = bwait_warp(bars, C::B_Q, 0, abort_flag, tmo, ROLE_MMA);
-      tc_fence_after();
-      auto next_slot = [&](int& slot) -> bool {
-        slot = it % C::SLOTS;
-        const uint32_t ph = (it / C::SLOTS) & 1;
-        ++it;
-        if (!bwait_warp(bars, C::B_KV_FULL + slot, ph, abort_flag, tmo, ROLE_MMA)) return false;
-        tc_fence_after();
-        return true;
-      };
-      auto issue_s = [&](int j) -> bool {
-        const uint32_t tS = tmem + 128 * (j & 1);
-        for (int s = 0; s < 4; ++s) {
-          int slot;
-          if (!next_slot(slot)) return false;
-          const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            // k-steps 4c .. 4c+3. DMAJOR: 16 head dims = 16 rows of 128 B (2048 B apart);
-            // row-major: 32-byte steps inside one 64-d box, boxes CHUNK_BYTES apart.
-            const uint32_t st = DMAJOR ? 128u : 2u;
-            const uint32_t qoff = DMAJOR ? static_cast<uint32_t>((8 * s + 4 * c) * 2048) >> 4
-                                         : static_cast<uint32_t>((2 * s + c) * CHUNK_BYTES) >> 4;
-            const uint32_t koff = soff + (DMAJOR ? static_cast<uint32_t>(4 * c * 2048) >> 4
-                                                 : static_cast<uint32_t>(c * CHUNK_BYTES) >> 4);
-            const uint64_t qa = dQ + qoff, kb = dK + koff;
-            mma4_ss_warp(tS, qa, qa + st, qa + 2 * st, qa + 3 * st, kb, kb + st, kb + 2 * st, kb + 3 * st, IDESC_QK,
-                         (s > 0 || c > 0) ? 1u : 0u);
-          }
-          tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + slot));
-        }
-        tc_commit_warp(bars + 8 * (C::B_S_FULL + (j & 1)));
-        return true;
-      };
-      auto issue_pv = [&](int j) -> bool {
-        if (!bwait_warp(bars, C::B_P_FULL + (j & 1), (j >> 1) & 1, abort_flag, tmo, ROLE_MMA)) return false;
-        tc_fence_after();
-        const uint32_t tP = tmem + 128 * (j & 1);
-        for (int s = 0; s < 2; ++s) {
-          int slot;
-          if (!next_slot(slot)) return false;
-          const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            // keys 64c .. 64c+63. DMAJOR (V K-major): 32-byte steps inside one 64-key
-            // box; row-major (V MN-major): 16 key rows = 2048 B apart.
-            const uint32_t st = DMAJOR ? 2u : 128u;
-            const uint64_t vb = dV + soff + (DMAJOR ? static_cast<uint32_t>(c * CHUNK_BYTES) >> 4
-                                                    : static_cast<uint32_t>(4 * c * 2048) >> 4);
-            mma4_ts_warp(tO + 128 * s, tP + 32 * c, vb, vb + st, vb + 2 * st, vb + 3 * st, IDESC_PV,
-                         (j > 0 || c > 0) ? 1u : 0u);
-          }
-          tc_commit_warp(bars + 8 * (C::B_KV_EMPTY + slot));
-        }
-        tc_commit_warp(bars + 8 * C::B_PV_DONE);
-        return true;
-      };
-      for (int j = 0; j <= n_tiles && ok; ++j) {
-        if (j < n_tiles) ok = issue_s(j);
-        if (ok && j > 0) ok = issue_pv(j - 1);
-      }
-      if (ok) {
-        tc_commit_warp(bars + 8 * C::B_O_FULL);
-      } else {
-        tc_commit_warp(bars + 8 * C::B_DRAIN);
-        wait_slow(bars + 8 * C::B_DRAIN, 0, drain_flag, 100000000ull, C::B_DRAIN, ROLE_MMA);
-      }
-    }
-    __syncwarp();
-  } else if (warp < 4) {
-    // ------------------------------------------------------------- softmax
-    const int row = warp * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tO = tmem + lane_off + 256;
-    const float sl2 = p.scale_log2;
-    const bool pos = sl2 >= 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int b = j & 1;
-      const uint32_t tS = tmem + lane_off + 128 * b;
-      if (!bwait_warp(bars, C::B_S_FULL + b, (j >> 1) & 1, abort_flag, tmo, ROLE_SOFTMAX0)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t s[BN];
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + 32 * c, s + 32 * c);
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) reg_fence32(s + 32 * c);
-      const int nvalid = min(BN, p.Skv - j * BN);
-      const bool full = nvalid == BN;
-      const float mx = row_extreme(s, nvalid, full, pos);
-      const float m_new = fmaxf(m_run, mx * sl2);
-      const bool need = m_new > m_run + RESCALE_THRESHOLD;
-      float factor = 1.f;
-      if (need) {
-        factor = ex2_approx(m_run - m_new);
-        m_run = m_new;
-      }
-      l_run *= factor;
-      float lsum0, lsum1;
-      if (full)
-        row_exp_store<false>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {}, [] {});
-      else
-        row_exp_store<true>(s, sl2, -m_run, nvalid, tS, lsum0, lsum1, 0u, [] {}, [] {});
-      l_run += lsum0 + lsum1;
-      // O may only be rescaled once PV(j-1) has completed.
-      if (j > 0) {
-        if (!bwait_warp(bars, C::B_PV_DONE, (j - 1) & 1, abort_flag, tmo, ROLE_SOFTMAX0)) { ok = false; break; }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, need)) {
-#pragma unroll 1
-          for (int c = 0; c < 256 / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + 32 * c, o);
-            tmem_wait_ld();
-            reg_fence32(o);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
-            tmem_st32(tO + 32 * c, o);
-          }
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bars + 8 * (C::B_P_FULL + b));
-    }
-    const bool have_o = ok && n_tiles > 0 && bwait_warp(bars, C::B_O_FULL, 0, abort_flag, tmo, ROLE_SOFTMAX0);
-    if (have_o) {
-      tc_fence_after();
-      const float inv = 1.f / l_run;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[64];
-        tmem_ld32(tO + 64 * c, o);
-        tmem_ld32(tO + 64 * c + 32, o + 32);
-        tmem_wait_ld();
-        reg_fence32(o);
-        reg_fence32(o + 32);
-        // Q is dead (its last MMA completed): it becomes the staging buffer
-        if (DMAJOR) {  // [256 d][128 rows] fp16, row `row` is column `row`
-#pragma unroll
-          for (int e = 0; e < 64; ++e)
-            st_shared_u16(sQ + ((64 * c + e) * BM + row) * 2, __half_as_ushort(__float2half_rn(__uint_as_float(o[e]) * inv)));
-        } else {
-          const uint32_t rowbase = sQ + c * CHUNK_BYTES + row * 128;
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const uint32_t a = pack_half2(__uint_as_float(o[8 * u + 0]) * inv, __uint_as_float(o[8 * u + 1]) * inv);
-            const uint32_t bb = pack_half2(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv);
-            const uint32_t cc = pack_half2(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv);
-            const uint32_t d = pack_half2(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv);
-            st_shared_v4(rowbase + ((u ^ (row & 7)) << 4), a, bb, cc, d);
-          }
-        }
-      }
-      fence_proxy_async_smem();
-    }
-    mbar_arrive(bars + 8 * C::B_EPI);
-    if (warp == 0 && lane == 0 && have_o && bwait(bars, C::B_EPI, 0, abort_flag, tmo, ROLE_SOFTMAX0)) {
-      if (DMAJOR)
-        tma_store_3d(&tm_o, sQ, q_row0, 256 * half, bh);  // one [128 rows x 256 d] box
-      else
-        for (int c = 0; c < 4; ++c) tma_store_3d(&tm_o, sQ + c * CHUNK_BYTES, 256 * half + 64 * c, q_row0, bh);
-      tma_store_commit();
-      tma_store_wait_read0();
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 5) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
 // ------------------------------------------------- D = 512 on CTA pairs
-// The head-dim-half split of attn_fwd_d512_kernel, run on 2-CTA clusters: a
-// work unit is two query tiles of one (batch, head) and one head-dim half,
-// one query tile per CTA. The even CTA (the leader) issues every MMA with
+// Head dim 512 (the reference's VAE mid-block path, attn_kernel.hip:525-708).
+// An fp32 O tile of 128 rows x 512 columns fills all of TMEM, so O is split
+// into two 256-column halves of the head dim, and both halves compute the
+// full S = Q K^T (K = 512): 1.5x the minimum tensor work, in exchange for no
+// traffic between the halves. TMEM per CTA: S double-buffered at [0,128) /
+// [128,256), the O half at [256,512); P of a key tile is written over the
+// first 64 columns of its S buffer; MMA order S(0), S(1), PV(0), S(2),
+// PV(1), ... so that the tensor core computes S(j+1) while the softmax works
+// on S(j).
+//
+// Work runs on 2-CTA clusters: a work unit is two query tiles of one (batch,
+// head) and one head-dim half, one query tile per CTA. The even CTA (the
+// leader) issues every MMA with
 // cta_group::2: M = 256 rows, 128 from each CTA's Q tile, D in each CTA's own
 // TMEM. Each CTA loads only half of the B operands into its shared memory:
 // keys 64 r .. 64 r + 63 of every K tile and head dims 128 r .. 128 r + 127
 // of its half of every V tile (r = CTA rank), so a CTA streams 96 KiB per key
 // tile instead of 192 KiB and its three 32 KiB ring slots each feed 1024
-// tensor cycles instead of 512 (measured on the single-CTA kernel: its MMA
-// warp waited 19% of the time for K/V data; here 11%).
+// tensor cycles instead of 512 (measured on B200: with one CTA per (query
+// tile, half) the MMA warp waited 19% of the time for K/V data; here 11%).
 //
 // Persistent: one cluster per SM pair walks a list of segments (unit, first
 // key tile, end key tile) with the schedule of attn_fwd_kernel (SegIter over
@@ -1421,6 +1096,13 @@ struct Unit512 {
   }
 };
 
+// DMAJOR: q, k, v and o are stored transposed, [B*H][D][S] with the sequence
+// contiguous -- a [b, c, h, w] feature map is exactly this with H = 1, D = c,
+// S = h*w -- and the kernel reads and writes that layout directly: Q and K
+// become MN-major MMA operands (64 sequence positions per 128-byte row, head
+// dims down the rows), V a K-major one, and O is staged as [256 d][128 rows]
+// and written with one unswizzled TMA store. Whole units only (no workspace).
+template <bool DMAJOR>
 __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
     attn_fwd_d512_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -1504,7 +1186,14 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
       // the Q buffer is free once this CTA's previous segment is finished with it
       if (!bwait_warp(bars, C::B_Q_EMPTY, (qseg & 1) ^ 1u, abort_flag, tmo, ROLE_PRODUCER)) { ok = false; break; }
       if (leader) mbar_arrive_expect_tx_warp(bars + 8 * C::B_Q, 2 * C::Q_BYTES);
-      for (int c = 0; c < 8; ++c) tma_load_3d_pair_warp(sQ + c * CHUNK_BYTES, &tm_q, lead_q, c * 64, u.q_row0, u.bh);
+      if (DMAJOR) {
+        // [64 rows x 256 dims] boxes: 64-row M block mb at 64 KiB * mb, one 128-byte row per head dim
+        for (int mb = 0; mb < 2; ++mb)
+          for (int dd = 0; dd < 2; ++dd)
+            tma_load_3d_pair_warp(sQ + mb * 65536 + dd * 32768, &tm_q, lead_q, u.q_row0 + 64 * mb, 256 * dd, u.bh);
+      } else {
+        for (int c = 0; c < 8; ++c) tma_load_3d_pair_warp(sQ + c * CHUNK_BYTES, &tm_q, lead_q, c * 64, u.q_row0, u.bh);
+      }
       ++qseg;
       for (int j = t0; j <= t1 && ok; ++j) {
         if (j < t1) {
@@ -1513,10 +1202,15 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
             int slot;
             uint32_t lf;
             if (!(ok = slot_begin(slot, lf))) break;
+            if (DMAJOR) {  // one [64 keys x 256 dims] box: a 128-byte row per head dim
+              tma_load_3d_pair_warp(sRing + slot * C::SLOT_BYTES, &tm_k, lf, j * BN + 64 * static_cast<int>(rank),
+                                    256 * s, u.bh);
+            } else {
 #pragma unroll
-            for (int b = 0; b < 4; ++b)
-              tma_load_3d_pair_warp(sRing + slot * C::SLOT_BYTES + b * 8192, &tm_k, lf, 256 * s + 64 * b,
-                                    j * BN + 64 * static_cast<int>(rank), u.bh);
+              for (int b = 0; b < 4; ++b)
+                tma_load_3d_pair_warp(sRing + slot * C::SLOT_BYTES + b * 8192, &tm_k, lf, 256 * s + 64 * b,
+                                      j * BN + 64 * static_cast<int>(rank), u.bh);
+            }
           }
         }
         if (j > t0 && ok) {
@@ -1525,9 +1219,14 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
           uint32_t lf;
           if (!(ok = slot_begin(slot, lf))) break;
 #pragma unroll
-          for (int b = 0; b < 2; ++b)
-            tma_load_3d_pair_warp(sRing + slot * C::SLOT_BYTES + b * CHUNK_BYTES, &tm_v, lf,
-                                  C::DH * u.half + 128 * static_cast<int>(rank) + 64 * b, (j - 1) * BN, u.bh);
+          for (int b = 0; b < 2; ++b) {
+            if (DMAJOR)  // [64 keys x 128 dims] boxes: keys 0-63, then 64-127
+              tma_load_3d_pair_warp(sRing + slot * C::SLOT_BYTES + b * CHUNK_BYTES, &tm_v, lf, (j - 1) * BN + 64 * b,
+                                    C::DH * u.half + 128 * static_cast<int>(rank), u.bh);
+            else         // [128 keys x 64 dims] boxes
+              tma_load_3d_pair_warp(sRing + slot * C::SLOT_BYTES + b * CHUNK_BYTES, &tm_v, lf,
+                                    C::DH * u.half + 128 * static_cast<int>(rank) + 64 * b, (j - 1) * BN, u.bh);
+          }
         }
       }
     }
@@ -1547,11 +1246,17 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
     __syncwarp();
   } else if (warp == 5 && leader) {
     // ----------------------------------------------------------- MMA issuer
-    constexpr uint32_t IDESC_QK = idesc_f16_f32(2 * BM, BN, 0, 0);     // M = 256 over the pair, N = 128 keys
-    constexpr uint32_t IDESC_PV = idesc_f16_f32(2 * BM, C::DH, 0, 1);  // N = 256 head dims of this half
-    const uint64_t dQ = sdesc_sw128(sQ, 16, 1024);
-    const uint64_t dK = sdesc_sw128(sRing, 16, 1024);             // K-major [64 keys x 64 dims] boxes
-    const uint64_t dV = sdesc_sw128(sRing, CHUNK_BYTES, 1024);    // MN-major, 64-dim blocks 16 KiB apart
+    // Row-major: Q and K K-major, V MN-major. DMAJOR: Q and K MN-major (Q's
+    // second 64-row M block 64 KiB on; a CTA's 64 keys are one N block), V
+    // K-major (keys 64-127 one 16 KiB box on).
+    constexpr uint32_t IDESC_QK = idesc_f16_f32(2 * BM, BN, DMAJOR ? 1 : 0, DMAJOR ? 1 : 0);  // M = 256, N = 128 keys
+    constexpr uint32_t IDESC_PV = idesc_f16_f32(2 * BM, C::DH, 0, DMAJOR ? 0 : 1);  // N = 256 head dims of this half
+    const uint64_t dQ = sdesc_sw128(sQ, DMAJOR ? 65536 : 16, 1024);
+    const uint64_t dK = sdesc_sw128(sRing, DMAJOR ? 8192 : 16, 1024);
+    const uint64_t dV = sdesc_sw128(sRing, DMAJOR ? 16 : CHUNK_BYTES, 1024);
+    // descriptor steps of 16 head dims (S) / 16 keys (PV), in 16-byte units
+    constexpr uint32_t QK_STEP = DMAJOR ? 128u : 2u;  // 16 rows of 128 B, or 32 B inside a row
+    constexpr uint32_t PV_STEP = DMAJOR ? 2u : 128u;
     const uint32_t tO = tmem + 256;
     constexpr uint16_t BOTH = 0x3;
     int it = 0, qseg = 0;
@@ -1572,11 +1277,14 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
         const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
-          // head dims 256 s + 64 b ..: Q chunk 4 s + b, K box b; 16 dims = 32 bytes
-          const uint64_t qa = dQ + (static_cast<uint32_t>((4 * s + b) * CHUNK_BYTES) >> 4);
+          // head dims 256 s + 64 b ..: row-major, Q chunk 4 s + b and K box b
+          // (16 dims = 32 bytes); DMAJOR, 128-byte rows 256 s + 64 b .. of Q
+          // and 64 b .. of the K slot (both 8 KiB per 64 dims)
+          const uint64_t qa = dQ + (DMAJOR ? static_cast<uint32_t>((256 * s + 64 * b) * 128) >> 4
+                                           : static_cast<uint32_t>((4 * s + b) * CHUNK_BYTES) >> 4);
           const uint64_t kb = dK + soff + (static_cast<uint32_t>(b * 8192) >> 4);
-          mma4_ss_pair_warp(tS, qa, qa + 2, qa + 4, qa + 6, kb, kb + 2, kb + 4, kb + 6, IDESC_QK,
-                            (s > 0 || b > 0) ? 1u : 0u);
+          mma4_ss_pair_warp(tS, qa, qa + QK_STEP, qa + 2 * QK_STEP, qa + 3 * QK_STEP, kb, kb + QK_STEP,
+                            kb + 2 * QK_STEP, kb + 3 * QK_STEP, IDESC_QK, (s > 0 || b > 0) ? 1u : 0u);
         }
         tc_commit_pair_mc_warp(bars + 8 * (C::B_KV_EMPTY + slot), BOTH);
       }
@@ -1594,9 +1302,11 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
       const uint32_t soff = static_cast<uint32_t>(slot * C::SLOT_BYTES) >> 4;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        // keys 64 c .. 64 c + 63: P columns 32 c .., V rows 2048 bytes per 16 keys
-        const uint64_t vb = dV + soff + (static_cast<uint32_t>(4 * c * 2048) >> 4);
-        mma4_ts_pair_warp(tO, tP + 32 * c, vb, vb + 128, vb + 256, vb + 384, IDESC_PV, (acc || c > 0) ? 1u : 0u);
+        // keys 64 c .. 64 c + 63: P columns 32 c ..; row-major, V rows 2048
+        // bytes per 16 keys; DMAJOR, the second 16 KiB box, 32 bytes per 16 keys
+        const uint64_t vb = dV + soff + (static_cast<uint32_t>(DMAJOR ? c * CHUNK_BYTES : 4 * c * 2048) >> 4);
+        mma4_ts_pair_warp(tO, tP + 32 * c, vb, vb + PV_STEP, vb + 2 * PV_STEP, vb + 3 * PV_STEP, IDESC_PV,
+                          (acc || c > 0) ? 1u : 0u);
       }
       tc_commit_pair_mc_warp(bars + 8 * (C::B_KV_EMPTY + slot), BOTH);
       tc_commit_pair_mc_warp(bars + 8 * (last ? C::B_O_FULL : C::B_PV_DONE), BOTH);
@@ -1707,6 +1417,13 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
           tmem_wait_ld();
           reg_fence32(o);
           reg_fence32(o + 32);
+          if (DMAJOR) {  // [256 dims][128 rows] fp16: this row is column `row`
+#pragma unroll
+            for (int e = 0; e < 64; ++e)
+              st_shared_u16(sQ + ((64 * c + e) * BM + row) * 2,
+                            __half_as_ushort(__float2half_rn(__uint_as_float(o[e]) * inv)));
+            continue;
+          }
           const uint32_t rowbase = sQ + c * CHUNK_BYTES + row * 128;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
@@ -1725,8 +1442,11 @@ __global__ void __launch_bounds__(Cfg512P::THREADS, 1)
         if (warp == 0) {
           // (the odd CTA of the last pair may hold rows past Sq only: nothing to store)
           if (lane == 0 && u.q_row0 < p.Sq) {
-            for (int c = 0; c < 4; ++c)
-              tma_store_3d(&tm_o, sQ + c * CHUNK_BYTES, C::DH * u.half + 64 * c, u.q_row0, u.bh);
+            if (DMAJOR)  // one [128 rows x 256 dims] box
+              tma_store_3d(&tm_o, sQ, u.q_row0, C::DH * u.half, u.bh);
+            else
+              for (int c = 0; c < 4; ++c)
+                tma_store_3d(&tm_o, sQ + c * CHUNK_BYTES, C::DH * u.half + 64 * c, u.q_row0, u.bh);
             tma_store_commit();
             tma_store_wait_read0();
           }
@@ -1981,11 +1701,9 @@ int check_device(int* dev_out) {
                              fa::Cfg<64>::SMEM_BYTES) != cudaSuccess ||
         cudaFuncSetAttribute(fa::attn_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              fa::Cfg<128>::SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(fa::attn_fwd_d512_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             fa::Cfg512::SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(fa::attn_fwd_d512_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             fa::Cfg512::SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(fa::attn_fwd_d512_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(fa::attn_fwd_d512_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             fa::Cfg512P::SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(fa::attn_fwd_d512_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              fa::Cfg512P::SMEM_BYTES) != cudaSuccess)
       return GFX906_B200_ECUDA;
     di.attrs_set = true;
@@ -2224,36 +1942,6 @@ int launch_dp(const void* q, const void* k, const void* v, void* o, long long BH
   return launch_combine(pl, prm, DP, D, D, 0, stream);
 }
 
-template <bool DMAJOR>
-int launch_d512(const void* q, const void* k, const void* v, void* o, long long BH, int Sq, int Skv,
-                float scale, cudaStream_t stream) {
-  CUtensorMap mq, mk, mv, mo;
-  if (DMAJOR) {
-    if (!make_map_dmajor(&mq, q, 512, Sq, BH, 64, 256, true) || !make_map_dmajor(&mk, k, 512, Skv, BH, 64, 128, true) ||
-        !make_map_dmajor(&mv, v, 512, Skv, BH, 64, 128, true) || !make_map_dmajor(&mo, o, 512, Sq, BH, fa::BM, 256, false))
-      return GFX906_B200_ECUDA;
-  } else if (!make_map(&mq, q, 512, Sq, BH, fa::BM) || !make_map(&mk, k, 512, Skv, BH, fa::BN) ||
-             !make_map(&mv, v, 512, Skv, BH, fa::BN) || !make_map(&mo, o, 512, Sq, BH, fa::BM)) {
-    return GFX906_B200_ECUDA;
-  }
-  fa::Params prm{};
-  prm.Sq = Sq;
-  prm.Skv = Skv;
-  prm.D = 512;
-  prm.scale_log2 = scale * 1.4426950408889634f;
-  prm.timeout_ns = timeout_ns_from_env();
-  const unsigned qtiles = static_cast<unsigned>((Sq + fa::BM - 1) / fa::BM);
-  for (long long off = 0; off < BH; off += 65535) {
-    const long long n = (BH - off) < 65535 ? (BH - off) : 65535;
-    prm.bh_offset = static_cast<int>(off);
-    dim3 grid(2 * qtiles, static_cast<unsigned>(n), 1);
-    const int rc = launch_pdl(fa::attn_fwd_d512_kernel<DMAJOR>, grid, dim3(fa::Cfg512::THREADS),
-                              fa::Cfg512::SMEM_BYTES, stream, 1, mq, mk, mv, mo, prm);
-    if (rc != GFX906_B200_OK) return rc;
-  }
-  return GFX906_B200_OK;
-}
-
 // Persistent schedule of attn_fwd_d512_pair_kernel: units are (batch x head,
 // query-tile pair, head-dim half), one cluster of two CTAs per SM pair.
 // Whole units first; with a workspace, the last partial wave's key range is
@@ -2302,16 +1990,25 @@ size_t workspace_bytes512(const Plan& pl) {
   return align256(slots * 2 * sizeof(float)) + slots * fa::Cfg512P::DH * sizeof(float);
 }
 
-// D = 512 (row-major) on CTA pairs: grid x = 2 x clusters, clusters of 2.
+// D = 512 on CTA pairs: grid x = 2 x clusters, clusters of 2. DMAJOR: the
+// transposed layout, whole units only (the workspace is ignored).
+template <bool DMAJOR>
 int launch_d512_pair(const void* q, const void* k, const void* v, void* o, long long BH, int Sq, int Skv,
                      float scale, void* ws, size_t ws_size, int dev, cudaStream_t stream) {
+  if (DMAJOR) ws = nullptr;
   Plan pl;
   if (!make_plan512(BH, Sq, Skv, device_sms(dev), ws != nullptr, &pl)) return GFX906_B200_EINVAL;
   if (BH > 0x7fffffffll) return GFX906_B200_EINVAL;
   CUtensorMap mq, mk, mv, mo;
-  if (!make_map(&mq, q, 512, Sq, BH, fa::BM) || !make_map(&mk, k, 512, Skv, BH, fa::BN / 2) ||
-      !make_map(&mv, v, 512, Skv, BH, fa::BN) || !make_map(&mo, o, 512, Sq, BH, fa::BM))
+  if (DMAJOR) {
+    if (!make_map_dmajor(&mq, q, 512, Sq, BH, 64, 256, true) || !make_map_dmajor(&mk, k, 512, Skv, BH, 64, 256, true) ||
+        !make_map_dmajor(&mv, v, 512, Skv, BH, 64, 128, true) ||
+        !make_map_dmajor(&mo, o, 512, Sq, BH, fa::BM, fa::Cfg512P::DH, false))
+      return GFX906_B200_ECUDA;
+  } else if (!make_map(&mq, q, 512, Sq, BH, fa::BM) || !make_map(&mk, k, 512, Skv, BH, fa::BN / 2) ||
+             !make_map(&mv, v, 512, Skv, BH, fa::BN) || !make_map(&mo, o, 512, Sq, BH, fa::BM)) {
     return GFX906_B200_ECUDA;
+  }
   fa::Params prm{};
   prm.Sq = Sq;
   prm.Skv = Skv;
@@ -2337,7 +2034,7 @@ int launch_d512_pair(const void* q, const void* k, const void* v, void* o, long 
     base += align256(slots * 2 * sizeof(float));
     prm.ws_o = reinterpret_cast<float*>(base);
   }
-  const int rc = launch_pdl(fa::attn_fwd_d512_pair_kernel, dim3(2 * static_cast<unsigned>(pl.G)),
+  const int rc = launch_pdl(fa::attn_fwd_d512_pair_kernel<DMAJOR>, dim3(2 * static_cast<unsigned>(pl.G)),
                             dim3(fa::Cfg512P::THREADS), fa::Cfg512P::SMEM_BYTES, stream, 2, mq, mk, mv, mo, prm);
   if (rc != GFX906_B200_OK || !pl.split) return rc;
   return launch_combine(pl, prm, fa::Cfg512P::DH, 512, fa::Cfg512P::DH, 1, stream);
@@ -2383,7 +2080,7 @@ int attn_launch_impl(const void* q, const void* k, const void* v, void* o, int B
   }
   if (D == 128) return launch_dp<128>(q, k, v, o, BH, Sq, Skv, D, scale, ws, ws_size, dev, stream);
   if (D <= 64) return launch_dp<64>(q, k, v, o, BH, Sq, Skv, D, scale, ws, ws_size, dev, stream);
-  return launch_d512_pair(q, k, v, o, BH, Sq, Skv, scale, ws, ws_size, dev, stream);
+  return launch_d512_pair<false>(q, k, v, o, BH, Sq, Skv, scale, ws, ws_size, dev, stream);
 }
 
 }  // namespace
@@ -2416,7 +2113,7 @@ int gfx906_b200_attn_launch_dmajor(const void* q, const void* k, const void* v, 
                    ? GFX906_B200_OK
                    : GFX906_B200_ECUDA;
         } else {
-          rc = launch_d512<true>(q, k, v, o, BH, Sq, Skv, scale, stream);
+          rc = launch_d512_pair<true>(q, k, v, o, BH, Sq, Skv, scale, nullptr, 0, dev, stream);
         }
       }
     }

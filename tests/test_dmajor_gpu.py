@@ -12,8 +12,10 @@ from tests.gpu_util import check_rows, sample_rows
 
 pytestmark = pytest.mark.gpu
 
+# CTA pairs of 2 x 128 query rows: one tile (the odd CTA past Sq), three
+# tiles (the second pair's odd CTA past Sq), ragged rows and keys, C4's heads
 SHAPES = [(1, 1, 1024, 1024), (2, 1, 1000, 1000), (1, 2, 256, 1032), (1, 1, 8, 16), (1, 3, 136, 264),
-          (1, 1, 4096, 4096)]
+          (1, 1, 4096, 4096), (1, 1, 384, 1000), (1, 4, 1024, 4096)]
 
 
 def dmajor(t):  # [B,H,S,D] -> contiguous [B,H,D,S]
