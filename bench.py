@@ -267,8 +267,12 @@ def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, 
     alone, the kernel alone on all SMs but `reserve_sms`, the broadcast alone,
     the gather alone, the three in sequence, and the three pipelined across
     calls (shard.attention_by_rows_pipelined: the next call's K/V broadcast
-    and this call's gather run beside the next kernel on the reserved SMs).
-    The legs run interleaved `reps` times; each figure is the best repeat."""
+    and this call's gather run beside the next kernel on the reserved SMs),
+    the same with K/V pulled on the copy engines instead of broadcast
+    (shard.attention_by_rows_copy_engine, the kernel on every SM, the NCCL
+    gather after it), and with the output rows pushed on the copy engines as
+    well (B * H == 1). The legs run interleaved `reps` times; each figure is
+    the best repeat."""
     import gfx906_b200
     from gfx906_b200 import shard
 
@@ -318,6 +322,51 @@ def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, 
                                                                 out=out_full) for _ in range(n)]),
         "pipelined": pipelined,
     }
+    # copy engines: K/V pulled from rank 0's ring over CUDA IPC while the
+    # previous call's kernel runs on every SM (gfx906_b200.peer.KVBroadcast);
+    # set up collectively, used only if it came up on every rank
+    ce, ce_error = None, None
+    if world > 1:
+        try:
+            from gfx906_b200.peer import KVBroadcast
+
+            ce = KVBroadcast(tuple(kd.shape), dtype=kd.dtype, src=0)
+            if rank == 0:  # the same K/V every call: both ring pairs hold them
+                for b in range(ce.depth):
+                    ce.k[b].copy_(kd)
+                    ce.v[b].copy_(vd)
+        except Exception as e:  # noqa: BLE001 - reported in the record
+            ce_error = f"{type(e).__name__}: {e}"
+        up = torch.tensor([0 if ce_error else 1], device=dev)
+        torch.distributed.all_reduce(up, op=torch.distributed.ReduceOp.MIN)
+        if int(up.item()) == 0:
+            ce_error = ce_error or "not available on another rank"
+            if ce is not None:
+                ce.close()
+            ce = None
+    rg = None
+    if ce is not None:
+        legs["pipelined_copy_engine"] = lambda n: shard.attention_by_rows_copy_engine(
+            [q_rows] * n, ce, cfg.scale, cfg.Sq, [obuf[i % 2] for i in range(n)])
+        if cfg.B * cfg.H == 1:
+            # the output rows pushed to every rank on the copy engines as well
+            from gfx906_b200.peer import RowGather
+
+            rows = [(shard.row_shard(cfg.Sq, r, world).start, shard.row_shard(cfg.Sq, r, world).stop)
+                    for r in range(world)]
+            try:
+                rg = RowGather(tuple(out_full.shape), rows)
+            except Exception as e:  # noqa: BLE001 - reported in the record
+                ce_error = f"row gather: {type(e).__name__}: {e}"
+            up = torch.tensor([0 if rg is None else 1], device=dev)
+            torch.distributed.all_reduce(up, op=torch.distributed.ReduceOp.MIN)
+            if int(up.item()) == 0:
+                if rg is not None:
+                    rg.close()
+                rg = None
+            else:
+                legs["copy_engine_all"] = lambda n: shard.attention_by_rows_copy_engine(
+                    [q_rows] * n, ce, cfg.scale, cfg.Sq, rg=rg)
     ms = {}
     for rep in range(reps):  # legs interleaved, best of `reps` (each the max over ranks)
         for name, fn in legs.items():  # every rank runs the same legs in the same order
@@ -337,6 +386,10 @@ def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, 
             barrier(world)
             t = max_over_ranks(e0.elapsed_time(e1), world) / steps
             ms[name] = min(ms.get(name, t), t)
+    if rg is not None:
+        rg.close()
+    if ce is not None:
+        ce.close()
     kv_bytes = 2 * kd.numel() * kd.element_size()
     o_bytes = out_full.numel() * out_full.element_size()
     return {
@@ -345,9 +398,16 @@ def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, 
         "kernel_ms": ms["kernel"], "kernel_reserved_ms": ms["kernel_reserved"], "reserve_sms": reserve_sms,
         "broadcast_ms": ms["broadcast"], "gather_ms": ms["gather"],
         "with_collectives_ms": ms["with_collectives"], "pipelined_ms": ms["pipelined"],
+        "pipelined_copy_engine_ms": ms.get("pipelined_copy_engine"),
+        "copy_engine_all_ms": ms.get("copy_engine_all"),
+        "copy_engine_error": ce_error,
         "value_kernel": cfg.flops / (ms["kernel"] * 1e-3) / 1e12,
         "value_with_collectives": cfg.flops / (ms["with_collectives"] * 1e-3) / 1e12,
         "value_pipelined": cfg.flops / (ms["pipelined"] * 1e-3) / 1e12,
+        "value_pipelined_copy_engine": (cfg.flops / (ms["pipelined_copy_engine"] * 1e-3) / 1e12
+                                        if "pipelined_copy_engine" in ms else None),
+        "value_copy_engine_all": (cfg.flops / (ms["copy_engine_all"] * 1e-3) / 1e12
+                                  if "copy_engine_all" in ms else None),
         "unit": UNIT,
         "collectives": (f"NCCL broadcast of K and V from rank 0 ({kv_bytes / 2**20:.0f} MiB) and "
                         f"all_gather_into_tensor of O ({o_bytes / 2**20:.0f} MiB) over {world} rank(s)"

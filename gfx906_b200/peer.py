@@ -1,0 +1,364 @@
+"""K/V broadcast on the copy engines, between the GPUs of one node.
+
+NCCL's collectives are kernels: while the persistent attention kernel holds
+every SM, a broadcast enqueued beside it cannot start, so query-row sharding
+(``shard.attention_by_rows``) pays for the broadcast of the next call's K and
+V on top of this call's kernel. A device-to-device copy that reads another
+GPU's memory runs on the copy engines instead and overlaps the kernel.
+
+``KVBroadcast`` keeps a ring of ``depth`` K/V buffer pairs on every rank. The
+source rank's buffers are mapped into the other ranks' address spaces with
+CUDA IPC (``cudaIpcGetMemHandle`` / ``cudaIpcOpenMemHandle``, opened on the
+rank's own device with lazy peer access), and each receiving rank pulls a
+call's K and V into its own pair with one ``cudaMemcpyAsync`` each on a
+copy stream: the data crosses NVLink once per receiver, into local memory,
+and the kernel reads it from there.
+
+Ordering across processes uses inter-process CUDA events plus keys in the
+process group's store. A rank records an event and only then publishes a key
+naming the call; a rank that needs that event waits for the key on the host
+before it enqueues the wait on the event, so it never waits on an older
+recording of the same event. Per call i (buffer pair b = i % depth):
+
+* source, ``source(i)``: the host waits for every receiver's "pulled i -
+  depth" key, the current stream waits for their pulled events: pair b may be
+  rewritten. The caller writes call i's K and V into the returned pair.
+* source, ``start(i)``: records "ready" for pair b on the current stream and
+  publishes "ready i".
+* receiver, ``start(i)``: waits for "ready i", makes the copy stream wait for
+  the source's ready event and for this rank's own last use of pair b
+  (``release``), pulls K and V, records "pulled" and publishes "pulled i".
+* every rank, ``wait(i)``: the current stream waits for call i's K/V;
+  returns the pair. ``release(i)`` after enqueuing the kernels that read it.
+
+Store waits carry the store's timeout, so a rank that died leaves the others
+with an error instead of a hang. No kernel of this module waits on another
+GPU, and nothing here uses multicast.
+"""
+
+from __future__ import annotations
+
+import itertools
+from typing import List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+_instances = itertools.count()
+
+
+def _rt():
+    try:
+        from cuda.bindings import driver, runtime
+    except ImportError as e:  # pragma: no cover - cuda-python ships with the image
+        raise RuntimeError(f"copy-engine transport needs cuda-python: {e}") from e
+    return runtime, driver
+
+
+def _check(res, what: str):
+    """Raises on a non-zero status; returns the call's outputs (None, one, or a tuple)."""
+    if not isinstance(res, tuple):
+        res = (res,)
+    err, out = res[0], res[1:]
+    if int(err) != 0:
+        raise RuntimeError(f"{what} failed: {err}")
+    if not out:
+        return None
+    return out[0] if len(out) == 1 else out
+
+
+def export_tensor(t: torch.Tensor) -> Tuple[bytes, int]:
+    """(IPC handle of the allocation holding t, byte offset of t in it)."""
+    rt, drv = _rt()
+    ptr = t.data_ptr()
+    base, _size = _check(drv.cuMemGetAddressRange(ptr), "cuMemGetAddressRange")
+    handle = _check(rt.cudaIpcGetMemHandle(int(base)), "cudaIpcGetMemHandle")
+    return bytes(handle.reserved), ptr - int(base)
+
+
+def open_handle(handle: bytes) -> int:
+    """Maps another process's allocation into this device's address space."""
+    rt, _ = _rt()
+    h = rt.cudaIpcMemHandle_t()
+    h.reserved = handle
+    return int(_check(rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle"))
+
+
+def close_handle(base: int) -> None:
+    rt, _ = _rt()
+    rt.cudaIpcCloseMemHandle(base)
+
+
+def copy_async(dst: int, src: int, nbytes: int, stream: int) -> None:
+    """cudaMemcpyAsync device to device (a peer source runs on a copy engine)."""
+    rt, _ = _rt()
+    _check(rt.cudaMemcpyAsync(dst, src, nbytes, rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice, stream),
+           "cudaMemcpyAsync")
+
+
+class _IpcEvent:
+    """An inter-process CUDA event (no timing), created here or opened from a handle."""
+
+    def __init__(self, handle: Optional[bytes] = None):
+        rt, _ = _rt()
+        self._rt = rt
+        if handle is None:
+            flags = rt.cudaEventInterprocess | rt.cudaEventDisableTiming
+            self.ev = _check(rt.cudaEventCreateWithFlags(flags), "cudaEventCreateWithFlags")
+            self.handle = bytes(_check(rt.cudaIpcGetEventHandle(self.ev), "cudaIpcGetEventHandle").reserved)
+        else:
+            h = rt.cudaIpcEventHandle_t()
+            h.reserved = handle
+            self.ev = _check(rt.cudaIpcOpenEventHandle(h), "cudaIpcOpenEventHandle")
+            self.handle = handle
+
+    def record(self, stream: int) -> None:
+        _check(self._rt.cudaEventRecord(self.ev, stream), "cudaEventRecord")
+
+    def wait_on(self, stream: int) -> None:
+        _check(self._rt.cudaStreamWaitEvent(stream, self.ev, 0), "cudaStreamWaitEvent")
+
+    def destroy(self) -> None:
+        self._rt.cudaEventDestroy(self.ev)
+
+
+class KVBroadcast:
+    """K and V of every call from rank `src` to all ranks of `group`, pulled
+    by the receivers on their copy engines (see the module docstring).
+
+    shape, dtype: one K (or V) tensor. depth: buffer pairs in the ring (2
+    lets call i + 1's transfer run during call i's kernel). Construction is
+    collective over `group` (an exchange of IPC handles)."""
+
+    def __init__(self, shape, dtype=torch.float16, src: int = 0, group=None, depth: int = 2,
+                 device: Optional[torch.device] = None, store=None):
+        if depth < 2:
+            raise ValueError("depth must be >= 2")
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.src, self.depth, self.group = src, depth, group
+        self.is_source = self.rank == src
+        self.receivers: List[int] = [r for r in range(self.world) if r != src]
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        ring = torch.empty((depth, 2) + tuple(shape), dtype=dtype, device=self.device)
+        self.k = [ring[b, 0] for b in range(depth)]
+        self.v = [ring[b, 1] for b in range(depth)]
+        self.nbytes = self.k[0].numel() * self.k[0].element_size()
+        # calls issued so far: call indices run on across uses, every rank alike
+        self.calls = 0
+        self.copy_stream = torch.cuda.Stream(self.device)
+        base_store = store or dist.distributed_c10d._get_default_store()
+        self.store = dist.PrefixStore(f"gfx906_b200/kv/{next(_instances)}/", base_store)
+        self._mapped: dict = {}
+        self._events: List[_IpcEvent] = []
+        with torch.cuda.device(self.device):
+            if self.is_source:
+                self.ready = [self._event() for _ in range(depth)]
+                handle, off = export_tensor(ring)
+                payload = {"ring": (handle, off), "ready": [e.handle for e in self.ready]}
+            else:
+                self.pulled = [self._event() for _ in range(depth)]
+                self.released = [torch.cuda.Event() for _ in range(depth)]
+                self.arrived = [torch.cuda.Event() for _ in range(depth)]
+                payload = {"pulled": [e.handle for e in self.pulled]}
+            payloads: list = [None] * self.world
+            dist.all_gather_object(payloads, payload, group=group)
+            if self.is_source:
+                self.peer_pulled = {r: [self._event(h) for h in payloads[r]["pulled"]] for r in self.receivers}
+            else:
+                handle, off = payloads[src]["ring"]
+                if handle not in self._mapped:
+                    self._mapped[handle] = open_handle(handle)
+                base = self._mapped[handle] + off
+                pair = 2 * self.nbytes
+                self.src_k = [base + b * pair for b in range(depth)]
+                self.src_v = [base + b * pair + self.nbytes for b in range(depth)]
+                self.src_ready = [self._event(h) for h in payloads[src]["ready"]]
+
+    def _event(self, handle: Optional[bytes] = None) -> _IpcEvent:
+        e = _IpcEvent(handle)
+        self._events.append(e)
+        return e
+
+    def source(self, i: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Source rank: the pair to write call i's K and V into, once every
+        receiver has pulled what the pair held before (the current stream
+        waits for that)."""
+        if not self.is_source:
+            raise RuntimeError("source() is for the source rank")
+        b = i % self.depth
+        if i >= self.depth and self.receivers:
+            old = i - self.depth
+            keys = [f"pulled/{r}/{old}" for r in self.receivers]
+            self.store.wait(keys)
+            cur = torch.cuda.current_stream(self.device).cuda_stream
+            for r in self.receivers:
+                self.peer_pulled[r][b].wait_on(cur)
+        return self.k[b], self.v[b]
+
+    def start(self, i: int) -> None:
+        """Source: call i's K/V are complete once the current stream reaches
+        this point. Receiver: enqueue the pull of call i's K/V."""
+        b = i % self.depth
+        if self.is_source:
+            self.ready[b].record(torch.cuda.current_stream(self.device).cuda_stream)
+            self.store.set(f"ready/{i}", b"1")
+            return
+        self.store.wait([f"ready/{i}"])
+        cs = self.copy_stream.cuda_stream
+        self.src_ready[b].wait_on(cs)
+        if i >= self.depth:
+            self.copy_stream.wait_event(self.released[b])
+        copy_async(self.k[b].data_ptr(), self.src_k[b], self.nbytes, cs)
+        copy_async(self.v[b].data_ptr(), self.src_v[b], self.nbytes, cs)
+        self.pulled[b].record(cs)
+        self.store.set(f"pulled/{self.rank}/{i}", b"1")
+        self.arrived[b].record(self.copy_stream)
+
+    def wait(self, i: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        """The current stream waits for call i's K/V; returns them."""
+        b = i % self.depth
+        if not self.is_source:
+            torch.cuda.current_stream(self.device).wait_event(self.arrived[b])
+        return self.k[b], self.v[b]
+
+    def release(self, i: int) -> None:
+        """Call after enqueuing the last kernel that reads call i's K/V."""
+        if not self.is_source:
+            self.released[i % self.depth].record(torch.cuda.current_stream(self.device))
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        for e in self._events:
+            e.destroy()
+        self._events = []
+        for base in self._mapped.values():
+            close_handle(base)
+        self._mapped = {}
+
+
+class RowGather:
+    """Every call's output assembled on every rank by the copy engines: each
+    rank pushes its block of query rows into the other ranks' output rings
+    (CUDA IPC) right after its kernel has written them, instead of an NCCL
+    all-gather (a kernel, which would have to wait for free SMs).
+
+    out_shape: [B, H, Sq, D] with B * H == 1 (a rank's row block is then one
+    contiguous range); rows: (start, stop) of every rank's block. Per call i
+    (ring slot b = i % depth):
+
+    * ``begin(i)``: this rank's slot b may be written by the other ranks
+      (recorded on the current stream, so after whatever consumed call
+      i - depth's output), and this rank's own push of call i - depth has
+      read its rows (the current stream waits);
+    * the kernel writes this rank's rows of ``out(i)`` (``rows_out(i)``);
+    * ``push(i)``: after that kernel, the copy stream waits for every other
+      rank's "begin i", then copies the rows into their slot b;
+    * ``complete(i)``: the current stream waits for every other rank's push
+      of call i: ``out(i)`` then holds the whole output until call i + depth
+      begins; or ``ack(i)`` when nobody reads call i's output: the host
+      only waits until every other rank has enqueued its push of call i.
+
+    One of the two must run for call i before ``begin(i + depth)``: a rank
+    re-records its "begin" and "pushed" events only after every other rank
+    has enqueued its wait on the previous recording. Construction is
+    collective over `group`."""
+
+    def __init__(self, out_shape, rows, dtype=torch.float16, group=None, depth: int = 2,
+                 device: Optional[torch.device] = None, store=None):
+        B, H, Sq, D = out_shape
+        if B * H != 1:
+            raise ValueError("RowGather needs B * H == 1 (contiguous row blocks)")
+        if depth < 2:
+            raise ValueError("depth must be >= 2")
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.depth, self.group = depth, group
+        self.peers = [r for r in range(self.world) if r != self.rank]
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.ring = torch.empty((depth,) + tuple(out_shape), dtype=dtype, device=self.device)
+        self.row_bytes = D * self.ring.element_size()
+        self.slot_bytes = Sq * self.row_bytes
+        self.start_row, self.stop_row = rows[self.rank]
+        self.copy_stream = torch.cuda.Stream(self.device)
+        self.calls = 0
+        base_store = store or dist.distributed_c10d._get_default_store()
+        self.store = dist.PrefixStore(f"gfx906_b200/rows/{next(_instances)}/", base_store)
+        self._mapped: dict = {}
+        self._events: List[_IpcEvent] = []
+        with torch.cuda.device(self.device):
+            self.pushed = [self._event() for _ in range(depth)]
+            self.freed = [self._event() for _ in range(depth)]
+            self.push_read = [torch.cuda.Event() for _ in range(depth)]
+            handle, off = export_tensor(self.ring)
+            payload = {"ring": (handle, off), "pushed": [e.handle for e in self.pushed],
+                       "freed": [e.handle for e in self.freed]}
+            payloads: list = [None] * self.world
+            dist.all_gather_object(payloads, payload, group=group)
+            self.peer_ring, self.peer_pushed, self.peer_freed = {}, {}, {}
+            for p in self.peers:
+                h, o = payloads[p]["ring"]
+                if h not in self._mapped:
+                    self._mapped[h] = open_handle(h)
+                self.peer_ring[p] = self._mapped[h] + o
+                self.peer_pushed[p] = [self._event(x) for x in payloads[p]["pushed"]]
+                self.peer_freed[p] = [self._event(x) for x in payloads[p]["freed"]]
+
+    def _event(self, handle: Optional[bytes] = None) -> _IpcEvent:
+        e = _IpcEvent(handle)
+        self._events.append(e)
+        return e
+
+    def out(self, i: int) -> torch.Tensor:
+        return self.ring[i % self.depth]
+
+    def rows_out(self, i: int) -> torch.Tensor:
+        return self.ring[i % self.depth][:, :, self.start_row:self.stop_row]
+
+    def begin(self, i: int) -> None:
+        b = i % self.depth
+        cur = torch.cuda.current_stream(self.device)
+        if i >= self.depth:
+            cur.wait_event(self.push_read[b])
+        self.freed[b].record(cur.cuda_stream)
+        self.store.set(f"freed/{self.rank}/{i}", b"1")
+
+    def push(self, i: int) -> None:
+        b = i % self.depth
+        cur = torch.cuda.current_stream(self.device)
+        written = torch.cuda.Event()
+        written.record(cur)
+        self.copy_stream.wait_event(written)
+        cs = self.copy_stream.cuda_stream
+        nbytes = (self.stop_row - self.start_row) * self.row_bytes
+        if self.peers and nbytes > 0:
+            self.store.wait([f"freed/{p}/{i}" for p in self.peers])
+            src = self.rows_out(i).data_ptr()
+            off = b * self.slot_bytes + self.start_row * self.row_bytes
+            for p in self.peers:
+                self.peer_freed[p][b].wait_on(cs)
+                copy_async(self.peer_ring[p] + off, src, nbytes, cs)
+        self.push_read[b].record(self.copy_stream)
+        self.pushed[b].record(cs)
+        self.store.set(f"pushed/{self.rank}/{i}", b"1")
+
+    def ack(self, i: int) -> None:
+        if self.peers:
+            self.store.wait([f"pushed/{p}/{i}" for p in self.peers])
+
+    def complete(self, i: int) -> torch.Tensor:
+        b = i % self.depth
+        self.ack(i)
+        cur = torch.cuda.current_stream(self.device).cuda_stream
+        for p in self.peers:
+            self.peer_pushed[p][b].wait_on(cur)
+        return self.out(i)
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        for e in self._events:
+            e.destroy()
+        self._events = []
+        for base in self._mapped.values():
+            close_handle(base)
+        self._mapped = {}

@@ -258,6 +258,79 @@ def attention_by_rows_pipelined(calls, Sq: int, src: int = 0, group=None, reserv
     return outs
 
 
+def attention_by_rows_copy_engine(q_rows_list, bc, scale, Sq: int, outs=None, group=None, fill=None, rg=None,
+                                  consume=None, local_attn: Optional[Callable] = None):
+    """A sequence of query-row sharded calls with K/V moved on the copy engines.
+
+    bc: a ``peer.KVBroadcast`` over `group` (its source rank holds K/V). Call
+    i's K and V reach every rank through bc's ring while call i - 1's kernel
+    runs: the transfer needs no SM, so the kernel keeps every SM. On the
+    source rank ``fill(i, k, v)`` writes call i's K/V into the ring pair (None:
+    the pairs already hold them).
+
+    Output, without `rg`: each call's rows are all-gathered (NCCL) into
+    ``outs[i]`` after its kernel; returns outs. With `rg` (a
+    ``peer.RowGather``; B * H == 1): the kernel writes this rank's rows into
+    rg's ring and they are pushed to the other ranks on the copy engines;
+    ``consume(i, out)`` gets call i's whole output once the current stream
+    has waited for it (valid until call i + rg.depth begins); without
+    `consume` only the last call's output is completed; returns it.
+    """
+    n = len(q_rows_list)
+    if n == 0:
+        return outs
+    world, rank = _group_world(group)
+    sh = row_shard(Sq, rank, world)
+    for q_rows in q_rows_list:
+        if q_rows.shape[2] != sh.size:
+            raise ValueError(f"rank {rank} holds {q_rows.shape[2]} query rows, its shard is {sh.size}")
+    if rg is not None:
+        if local_attn is not None:
+            raise ValueError("rg writes through the operator's attn_out; local_attn is not supported with it")
+        import gfx906_b200
+
+        attn_out = gfx906_b200._module_or_raise().attn_out
+        j0 = rg.calls
+        rg.calls += n
+    else:
+        attn = local_attn or _default_attn()
+    i0 = bc.calls  # the rings' call indices continue from earlier uses
+    bc.calls += n
+
+    def begin(i):
+        if bc.is_source:
+            k, v = bc.source(i0 + i)
+            if fill is not None:
+                fill(i, k, v)
+        bc.start(i0 + i)
+
+    last = None
+    begin(0)
+    for i in range(n):
+        k, v = bc.wait(i0 + i)
+        if i + 1 < n:
+            begin(i + 1)
+        if rg is None:
+            local = attn(q_rows_list[i], k, v, scale) if sh.size > 0 else q_rows_list[i].new_zeros(
+                q_rows_list[i].shape)
+            bc.release(i0 + i)
+            gather_rows(local, Sq, outs[i], group=group)
+            continue
+        j = j0 + i
+        rg.begin(j)
+        if sh.size > 0:
+            attn_out(q_rows_list[i], k, v, scale, rg.rows_out(j))
+        bc.release(i0 + i)
+        rg.push(j)
+        if consume is not None:
+            consume(i, rg.complete(j))
+        elif i + 1 == n:
+            last = rg.complete(j)
+        else:
+            rg.ack(j)
+    return outs if rg is None else last
+
+
 def choose_partition(B: int, H: int, world: int) -> str:
     """"heads" while every rank gets at least one (batch x head) unit, else "rows"."""
     return "heads" if B * H >= world else "rows"

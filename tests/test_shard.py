@@ -53,6 +53,9 @@ def _worker(rank, world, port, mode, result_q):
         if mode == "pipelined":
             _pipelined(rank, world, result_q)
             return
+        if mode == "copy_engine":
+            _copy_engine(rank, world, result_q)
+            return
         B, H, Sq, Skv, D = {"heads": (2, 3, 300, 257, 64), "rows": (1, 1, 1100, 700, 64),
                             "rows_eq": (1, 1, 256 * world * 2, 700, 64), "rows_bh": (2, 3, 512 * world, 300, 32),
                             "auto": (1, 2, 800, 300, 32)}[mode]
@@ -78,6 +81,66 @@ def _worker(rank, world, port, mode, result_q):
             result_q.put(float((out.float() - ref.float()).abs().max()))
     finally:
         dist.destroy_process_group()
+
+
+class _FakeKV:
+    """Stand-in for peer.KVBroadcast on CPU: the same call protocol (source,
+    start, wait, release, running call indices), the transfer a gloo
+    broadcast inside start()."""
+
+    def __init__(self, shape, src=0, depth=2):
+        self.is_source = dist.get_rank() == src
+        self.src, self.depth, self.calls = src, depth, 0
+        self.k = [torch.zeros(shape, dtype=torch.float16) for _ in range(depth)]
+        self.v = [torch.zeros(shape, dtype=torch.float16) for _ in range(depth)]
+        self.log = []
+
+    def source(self, i):
+        self.log.append(("source", i))
+        return self.k[i % self.depth], self.v[i % self.depth]
+
+    def start(self, i):
+        self.log.append(("start", i))
+        dist.broadcast(self.k[i % self.depth], src=self.src)
+        dist.broadcast(self.v[i % self.depth], src=self.src)
+
+    def wait(self, i):
+        self.log.append(("wait", i))
+        return self.k[i % self.depth], self.v[i % self.depth]
+
+    def release(self, i):
+        self.log.append(("release", i))
+
+
+def _copy_engine(rank, world, result_q):
+    """attention_by_rows_copy_engine over a fake broadcaster, used twice: the
+    outputs equal the unsharded results, call i + 1 is started before call
+    i's kernel, and call indices run on across uses."""
+    Sq, Skv, D = 256 * world * 2, 300, 64
+    scale = D ** -0.5
+    inputs = [make_qkv(1, 1, Sq, Skv, D, seed=40 + i) for i in range(3)]
+    sh = shard.row_shard(Sq, rank, world)
+    bc = _FakeKV((1, 1, Skv, D))
+
+    def fill(i, k, v):
+        k.copy_(inputs[i][1])
+        v.copy_(inputs[i][2])
+
+    err = 0.0
+    for use in range(2):
+        outs = [torch.full((1, 1, Sq, D), float("nan"), dtype=torch.float16) for _ in range(3)]
+        shard.attention_by_rows_copy_engine([x[0][:, :, sh.start:sh.stop].contiguous() for x in inputs], bc, scale,
+                                            Sq, outs, fill=fill, local_attn=oracle_attn)
+        for (q, k, v), out in zip(inputs, outs):
+            err = max(err, float((out.float() - oracle_attn(q, k, v, scale).float()).abs().max()))
+    starts = [i for op, i in bc.log if op == "start"]
+    assert starts == list(range(6)), starts
+    # within a use, the next call's transfer is enqueued before this call's
+    # kernel is released
+    for i in (0, 1, 3, 4):
+        assert bc.log.index(("start", i + 1)) < bc.log.index(("release", i))
+    if rank == 0:
+        result_q.put(err)
 
 
 def _pipelined(rank, world, result_q):
@@ -110,7 +173,8 @@ def _pipelined(rank, world, result_q):
 
 @pytest.mark.parametrize("mode,world", [("heads", 2), ("rows", 2), ("rows", 3), ("heads", 3), ("auto", 2),
                                         ("auto", 3), ("rows_eq", 2), ("rows_eq", 3), ("rows_bh", 2),
-                                        ("pipelined", 2), ("pipelined", 3)])
+                                        ("pipelined", 2), ("pipelined", 3), ("copy_engine", 2),
+                                        ("copy_engine", 3)])
 def test_sharded_attention_matches_unsharded(mode, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()

@@ -76,6 +76,39 @@ def _worker(rank, world, port, result_q):
         for (q, k, v), out in zip(ins, outs):
             full = gfx906_b200.attn(q.cuda(), k.cuda(), v.cuda(), D ** -0.5)
             errs.append(float((out.float() - full.float()).abs().max()))
+        # copy engines: the same 3 calls, K/V pulled from rank 0's ring over
+        # CUDA IPC while the previous kernel runs (fill writes each call's
+        # K/V into the ring on rank 0); the kernel keeps every SM
+        from gfx906_b200.peer import KVBroadcast
+
+        bc = KVBroadcast((1, 1, Skv, D), src=0)
+        dev_kv = [(k.cuda(), v.cuda()) for (_, k, v) in ins] if rank == 0 else None
+
+        def fill(i, kk, vv):
+            kk.copy_(dev_kv[i][0])
+            vv.copy_(dev_kv[i][1])
+
+        outs = [torch.full((1, 1, Sq, D), float("nan"), dtype=torch.float16, device="cuda") for _ in ins]
+        shard.attention_by_rows_copy_engine([c[0] for c in calls], bc, D ** -0.5, Sq, outs, fill=fill)
+        for (q, k, v), out in zip(ins, outs):
+            full = gfx906_b200.attn(q.cuda(), k.cuda(), v.cuda(), D ** -0.5)
+            errs.append(float((out.float() - full.float()).abs().max()))
+        # and with the output rows pushed to every rank on the copy engines too
+        from gfx906_b200.peer import RowGather
+
+        rows = [(shard.row_shard(Sq, r, world).start, shard.row_shard(Sq, r, world).stop) for r in range(world)]
+        rg = RowGather((1, 1, Sq, D), rows)
+        got = {}
+        shard.attention_by_rows_copy_engine([c[0] for c in calls], bc, D ** -0.5, Sq, fill=fill, rg=rg,
+                                            consume=lambda i, o: got.__setitem__(i, o.clone()))
+        last = shard.attention_by_rows_copy_engine([c[0] for c in calls], bc, D ** -0.5, Sq, fill=fill, rg=rg)
+        for i, (q, k, v) in enumerate(ins):
+            full = gfx906_b200.attn(q.cuda(), k.cuda(), v.cuda(), D ** -0.5)
+            errs.append(float((got[i].float() - full.float()).abs().max()))
+            if i == len(ins) - 1:
+                errs.append(float((last.float() - full.float()).abs().max()))
+        rg.close()
+        bc.close()
         torch.cuda.synchronize()
         if rank == 0:
             result_q.put(errs)
@@ -92,4 +125,4 @@ def test_sharded_attention_nccl():
     q = ctx.Queue()
     mp.start_processes(_worker, args=(world, _free_port(), q), nprocs=world, start_method="spawn", join=True)
     errs = q.get(timeout=120)
-    assert all(e <= 2e-3 for e in errs) and len(errs) == 6, errs
+    assert all(e <= 2e-3 for e in errs) and len(errs) == 13, errs
