@@ -14,37 +14,44 @@ call's K and V into its own pair with one ``cudaMemcpyAsync`` each on a
 copy stream: the data crosses NVLink once per receiver, into local memory,
 and the kernel reads it from there.
 
-Ordering across processes uses inter-process CUDA events plus keys in the
-process group's store. A rank records an event and only then publishes a key
-naming the call; a rank that needs that event waits for the key on the host
-before it enqueues the wait on the event, so it never waits on an older
-recording of the same event. Per call i (buffer pair b = i % depth):
+Ordering across processes uses inter-process CUDA events plus per-rank call
+counters in host shared memory (``Board``). A rank records an event and only
+then publishes the call's index; a rank that needs that event waits for the
+index on the host before it enqueues the wait on the event, so it never
+waits on an older recording of the same event. Per call i (buffer pair b =
+i % depth):
 
-* source, ``source(i)``: the host waits for every receiver's "pulled i -
-  depth" key, the current stream waits for their pulled events: pair b may be
-  rewritten. The caller writes call i's K and V into the returned pair.
+* source, ``source(i)``: the host waits until every receiver has published
+  "pulled i - depth", the current stream waits for their pulled events: pair
+  b may be rewritten. The caller writes call i's K and V into the returned pair.
 * source, ``start(i)``: records "ready" for pair b on the current stream and
   publishes "ready i".
-* receiver, ``start(i)``: waits for "ready i", makes the copy stream wait for
+* receiver, ``start(i)``: waits until "ready i" is published, makes the copy stream wait for
   the source's ready event and for this rank's own last use of pair b
   (``release``), pulls K and V, records "pulled" and publishes "pulled i".
 * every rank, ``wait(i)``: the current stream waits for call i's K/V;
   returns the pair. ``release(i)`` after enqueuing the kernels that read it.
 
-Store waits carry the store's timeout, so a rank that died leaves the others
-with an error instead of a hang. No kernel of this module waits on another
-GPU, and nothing here uses multicast.
+``RowGather`` does the reverse for the output: every rank pushes its block
+of query rows into the other ranks' output rings.
+
+Host waits carry a time limit, so a rank that died leaves the others with an
+error instead of a hang. No kernel of this module waits on another GPU, and
+nothing here uses multicast. All ranks must be on one node (CUDA IPC and the
+shared-memory board both need it).
 """
 
 from __future__ import annotations
 
-import itertools
+import time
 from typing import List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
 
-_instances = itertools.count()
+# Board channels of KVBroadcast and RowGather
+_READY, _PULLED = 0, 1
+_FREED, _PUSHED = 0, 1
 
 
 def _rt():
@@ -122,6 +129,66 @@ class _IpcEvent:
         self._rt.cudaEventDestroy(self.ev)
 
 
+class Board:
+    """Per-rank, per-channel monotonic counters in host shared memory, for
+    ranks on one node: ``publish(ch, i)`` sets this rank's counter of channel
+    ch to i + 1 (calls are published in increasing order), ``wait(ch, ranks,
+    i)`` returns once every listed rank has published call i. A round trip is
+    a few microseconds, against tens for a key in the process group's store,
+    which matters at several handshakes per call and call times of a tenth of
+    a millisecond. A wait gives up with TimeoutError after `timeout_s`, so a
+    rank that died leaves the others with an error instead of a hang.
+    Construction is collective over `group` (rank 0 creates the segment and
+    removes its name once every rank has mapped it)."""
+
+    def __init__(self, channels: int, group=None, timeout_s: float = 120.0):
+        import numpy as np
+        from multiprocessing import resource_tracker, shared_memory
+
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.timeout_s = timeout_s
+        size = 8 * channels * self.world
+        shm = shared_memory.SharedMemory(create=True, size=size) if self.rank == 0 else None
+        names: list = [None] * self.world
+        dist.all_gather_object(names, shm.name if shm is not None else None, group=group)
+        if shm is None:
+            shm = shared_memory.SharedMemory(name=names[0])
+            # the creator owns the segment; this process must not unlink it at exit
+            resource_tracker.unregister(shm._name, "shared_memory")  # noqa: SLF001
+        self._shm = shm
+        self.arr = np.ndarray((channels, self.world), dtype=np.int64, buffer=shm.buf)
+        if self.rank == 0:
+            self.arr[:] = 0
+        dist.barrier(group=group)
+        if self.rank == 0:
+            shm.unlink()  # every rank has it mapped; the name is no longer needed
+
+    def publish(self, ch: int, i: int) -> None:
+        self.arr[ch, self.rank] = i + 1
+
+    def wait(self, ch: int, ranks, i: int) -> None:
+        row = self.arr[ch]
+        need = i + 1
+        pending = [r for r in ranks if row[r] < need]
+        if not pending:
+            return
+        deadline = time.monotonic() + self.timeout_s
+        n = 0
+        while pending:
+            pending = [r for r in pending if row[r] < need]
+            n += 1
+            if n > 32:
+                time.sleep(0)
+            if (n & 1023) == 0 and time.monotonic() > deadline:
+                raise TimeoutError(f"rank(s) {pending} did not publish call {i} on channel {ch} "
+                                   f"within {self.timeout_s} s")
+
+    def close(self) -> None:
+        self.arr = None
+        self._shm.close()
+
+
 class KVBroadcast:
     """K and V of every call from rank `src` to all ranks of `group`, pulled
     by the receivers on their copy engines (see the module docstring).
@@ -131,7 +198,7 @@ class KVBroadcast:
     collective over `group` (an exchange of IPC handles)."""
 
     def __init__(self, shape, dtype=torch.float16, src: int = 0, group=None, depth: int = 2,
-                 device: Optional[torch.device] = None, store=None):
+                 device: Optional[torch.device] = None):
         if depth < 2:
             raise ValueError("depth must be >= 2")
         self.world = dist.get_world_size(group)
@@ -147,8 +214,7 @@ class KVBroadcast:
         # calls issued so far: call indices run on across uses, every rank alike
         self.calls = 0
         self.copy_stream = torch.cuda.Stream(self.device)
-        base_store = store or dist.distributed_c10d._get_default_store()
-        self.store = dist.PrefixStore(f"gfx906_b200/kv/{next(_instances)}/", base_store)
+        self.board = Board(2, group)  # channels READY (source), PULLED (receivers)
         self._mapped: dict = {}
         self._events: List[_IpcEvent] = []
         with torch.cuda.device(self.device):
@@ -188,9 +254,7 @@ class KVBroadcast:
             raise RuntimeError("source() is for the source rank")
         b = i % self.depth
         if i >= self.depth and self.receivers:
-            old = i - self.depth
-            keys = [f"pulled/{r}/{old}" for r in self.receivers]
-            self.store.wait(keys)
+            self.board.wait(_PULLED, self.receivers, i - self.depth)
             cur = torch.cuda.current_stream(self.device).cuda_stream
             for r in self.receivers:
                 self.peer_pulled[r][b].wait_on(cur)
@@ -202,9 +266,9 @@ class KVBroadcast:
         b = i % self.depth
         if self.is_source:
             self.ready[b].record(torch.cuda.current_stream(self.device).cuda_stream)
-            self.store.set(f"ready/{i}", b"1")
+            self.board.publish(_READY, i)
             return
-        self.store.wait([f"ready/{i}"])
+        self.board.wait(_READY, [self.src], i)
         cs = self.copy_stream.cuda_stream
         self.src_ready[b].wait_on(cs)
         if i >= self.depth:
@@ -212,7 +276,7 @@ class KVBroadcast:
         copy_async(self.k[b].data_ptr(), self.src_k[b], self.nbytes, cs)
         copy_async(self.v[b].data_ptr(), self.src_v[b], self.nbytes, cs)
         self.pulled[b].record(cs)
-        self.store.set(f"pulled/{self.rank}/{i}", b"1")
+        self.board.publish(_PULLED, i)
         self.arrived[b].record(self.copy_stream)
 
     def wait(self, i: int) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -235,6 +299,7 @@ class KVBroadcast:
         for base in self._mapped.values():
             close_handle(base)
         self._mapped = {}
+        self.board.close()
 
 
 class RowGather:
@@ -265,7 +330,7 @@ class RowGather:
     collective over `group`."""
 
     def __init__(self, out_shape, rows, dtype=torch.float16, group=None, depth: int = 2,
-                 device: Optional[torch.device] = None, store=None):
+                 device: Optional[torch.device] = None):
         B, H, Sq, D = out_shape
         if B * H != 1:
             raise ValueError("RowGather needs B * H == 1 (contiguous row blocks)")
@@ -282,8 +347,7 @@ class RowGather:
         self.start_row, self.stop_row = rows[self.rank]
         self.copy_stream = torch.cuda.Stream(self.device)
         self.calls = 0
-        base_store = store or dist.distributed_c10d._get_default_store()
-        self.store = dist.PrefixStore(f"gfx906_b200/rows/{next(_instances)}/", base_store)
+        self.board = Board(2, group)  # channels FREED, PUSHED
         self._mapped: dict = {}
         self._events: List[_IpcEvent] = []
         with torch.cuda.device(self.device):
@@ -321,7 +385,7 @@ class RowGather:
         if i >= self.depth:
             cur.wait_event(self.push_read[b])
         self.freed[b].record(cur.cuda_stream)
-        self.store.set(f"freed/{self.rank}/{i}", b"1")
+        self.board.publish(_FREED, i)
 
     def push(self, i: int) -> None:
         b = i % self.depth
@@ -332,7 +396,7 @@ class RowGather:
         cs = self.copy_stream.cuda_stream
         nbytes = (self.stop_row - self.start_row) * self.row_bytes
         if self.peers and nbytes > 0:
-            self.store.wait([f"freed/{p}/{i}" for p in self.peers])
+            self.board.wait(_FREED, self.peers, i)
             src = self.rows_out(i).data_ptr()
             off = b * self.slot_bytes + self.start_row * self.row_bytes
             for p in self.peers:
@@ -340,11 +404,11 @@ class RowGather:
                 copy_async(self.peer_ring[p] + off, src, nbytes, cs)
         self.push_read[b].record(self.copy_stream)
         self.pushed[b].record(cs)
-        self.store.set(f"pushed/{self.rank}/{i}", b"1")
+        self.board.publish(_PUSHED, i)
 
     def ack(self, i: int) -> None:
         if self.peers:
-            self.store.wait([f"pushed/{p}/{i}" for p in self.peers])
+            self.board.wait(_PUSHED, self.peers, i)
 
     def complete(self, i: int) -> torch.Tensor:
         b = i % self.depth
@@ -362,3 +426,4 @@ class RowGather:
         for base in self._mapped.values():
             close_handle(base)
         self._mapped = {}
+        self.board.close()
