@@ -341,9 +341,7 @@ def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, 
         torch.distributed.all_reduce(up, op=torch.distributed.ReduceOp.MIN)
         if int(up.item()) == 0:
             ce_error = ce_error or "not available on another rank"
-            if ce is not None:
-                ce.close()
-            ce = None
+            ce = None  # not closed: close() is collective and the other rank has none
     rg = None
     if ce is not None:
         legs["pipelined_copy_engine"] = lambda n: shard.attention_by_rows_copy_engine(
@@ -361,9 +359,7 @@ def strong_rows(cfg: AttnConfig, rank: int, world: int, local: int, steps: int, 
             up = torch.tensor([0 if rg is None else 1], device=dev)
             torch.distributed.all_reduce(up, op=torch.distributed.ReduceOp.MIN)
             if int(up.item()) == 0:
-                if rg is not None:
-                    rg.close()
-                rg = None
+                rg = None  # not closed: close() is collective and another rank has none
             else:
                 legs["copy_engine_all"] = lambda n: shard.attention_by_rows_copy_engine(
                     [q_rows] * n, ce, cfg.scale, cfg.Sq, rg=rg)

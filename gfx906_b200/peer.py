@@ -213,6 +213,7 @@ class KVBroadcast:
         self.nbytes = self.k[0].numel() * self.k[0].element_size()
         # calls issued so far: call indices run on across uses, every rank alike
         self.calls = 0
+        self._sourced = -1
         self.copy_stream = torch.cuda.Stream(self.device)
         self.board = Board(2, group)  # channels READY (source), PULLED (receivers)
         self._mapped: dict = {}
@@ -253,6 +254,7 @@ class KVBroadcast:
         if not self.is_source:
             raise RuntimeError("source() is for the source rank")
         b = i % self.depth
+        self._sourced = i
         if i >= self.depth and self.receivers:
             self.board.wait(_PULLED, self.receivers, i - self.depth)
             cur = torch.cuda.current_stream(self.device).cuda_stream
@@ -265,6 +267,8 @@ class KVBroadcast:
         this point. Receiver: enqueue the pull of call i's K/V."""
         b = i % self.depth
         if self.is_source:
+            if self._sourced != i:  # the pair must be free of call i - depth's pulls first
+                self.source(i)
             self.ready[b].record(torch.cuda.current_stream(self.device).cuda_stream)
             self.board.publish(_READY, i)
             return
@@ -292,7 +296,10 @@ class KVBroadcast:
             self.released[i % self.depth].record(torch.cuda.current_stream(self.device))
 
     def close(self) -> None:
+        """Collective: every rank's copies are done before any buffer or
+        mapping goes away."""
         torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
         for e in self._events:
             e.destroy()
         self._events = []
@@ -419,7 +426,10 @@ class RowGather:
         return self.out(i)
 
     def close(self) -> None:
+        """Collective: every rank's copies are done before any buffer or
+        mapping goes away."""
         torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
         for e in self._events:
             e.destroy()
         self._events = []
