@@ -361,6 +361,7 @@ class RowGather:
             self.pushed = [self._event() for _ in range(depth)]
             self.freed = [self._event() for _ in range(depth)]
             self.push_read = [torch.cuda.Event() for _ in range(depth)]
+            self.written = [torch.cuda.Event() for _ in range(depth)]
             handle, off = export_tensor(self.ring)
             payload = {"ring": (handle, off), "pushed": [e.handle for e in self.pushed],
                        "freed": [e.handle for e in self.freed]}
@@ -397,9 +398,8 @@ class RowGather:
     def push(self, i: int) -> None:
         b = i % self.depth
         cur = torch.cuda.current_stream(self.device)
-        written = torch.cuda.Event()
-        written.record(cur)
-        self.copy_stream.wait_event(written)
+        self.written[b].record(cur)
+        self.copy_stream.wait_event(self.written[b])
         cs = self.copy_stream.cuda_stream
         nbytes = (self.stop_row - self.start_row) * self.row_bytes
         if self.peers and nbytes > 0:
