@@ -6,29 +6,31 @@ every SM, a broadcast enqueued beside it cannot start, so query-row sharding
 V on top of this call's kernel. A device-to-device copy that reads another
 GPU's memory runs on the copy engines instead and overlaps the kernel.
 
-``KVBroadcast`` keeps a ring of ``depth`` K/V buffer pairs on every rank. The
-source rank's buffers are mapped into the other ranks' address spaces with
-CUDA IPC (``cudaIpcGetMemHandle`` / ``cudaIpcOpenMemHandle``, opened on the
-rank's own device with lazy peer access), and each receiving rank pulls a
-call's K and V into its own pair with one ``cudaMemcpyAsync`` each on a
-copy stream: the data crosses NVLink once per receiver, into local memory,
-and the kernel reads it from there.
+``KVBroadcast`` keeps a ring of ``depth`` K/V buffer pairs on every rank,
+mapped into the neighbouring ranks' address spaces with CUDA IPC
+(``cudaIpcGetMemHandle`` / ``cudaIpcOpenMemHandle``, opened on the rank's
+own device with lazy peer access). The ranks form a tree rooted at the
+source (by default every other rank is the source's child); each rank pulls
+a call's K and V from its parent's ring into its own with one
+``cudaMemcpyAsync`` each on a copy stream: the data crosses NVLink once per
+rank, into local memory, and the kernel reads it from there.
 
 Ordering across processes uses inter-process CUDA events plus per-rank call
 counters in host shared memory (``Board``). A rank records an event and only
 then publishes the call's index; a rank that needs that event waits for the
 index on the host before it enqueues the wait on the event, so it never
 waits on an older recording of the same event. Per call i (buffer pair b =
-i % depth):
+i % depth), with "have" the event a rank records once its pair b holds call
+i:
 
-* source, ``source(i)``: the host waits until every receiver has published
-  "pulled i - depth", the current stream waits for their pulled events: pair
-  b may be rewritten. The caller writes call i's K and V into the returned pair.
-* source, ``start(i)``: records "ready" for pair b on the current stream and
-  publishes "ready i".
-* receiver, ``start(i)``: waits until "ready i" is published, makes the copy stream wait for
-  the source's ready event and for this rank's own last use of pair b
-  (``release``), pulls K and V, records "pulled" and publishes "pulled i".
+* source, ``source(i)``: the host waits until every child has published
+  "have i - depth", the current stream waits for their events: pair b may
+  be rewritten. The caller writes call i's K and V into the returned pair.
+* source, ``start(i)``: records "have" on the current stream and publishes i.
+* other ranks, ``start(i)``: wait until the parent has published i; the
+  copy stream waits for the parent's "have", for the children's "have" of
+  call i - depth and for this rank's own last use of pair b (``release``),
+  pulls K and V, records "have" and publishes i.
 * every rank, ``wait(i)``: the current stream waits for call i's K/V;
   returns the pair. ``release(i)`` after enqueuing the kernels that read it.
 
@@ -50,7 +52,7 @@ import torch
 import torch.distributed as dist
 
 # Board channels of KVBroadcast and RowGather
-_READY, _PULLED = 0, 1
+_HAVE = 0
 _FREED, _PUSHED = 0, 1
 
 
@@ -191,21 +193,35 @@ class Board:
 
 class KVBroadcast:
     """K and V of every call from rank `src` to all ranks of `group`, pulled
-    by the receivers on their copy engines (see the module docstring).
+    on the copy engines (see the module docstring).
+
+    The ranks form a tree rooted at `src` with `fanout` children per rank
+    (default: every other rank is a child of the source). A rank pulls each
+    call's K and V from its parent's ring into its own, and its children
+    pull from it once it has them, so the source serves `fanout` pulls per
+    call instead of world - 1. One inter-process event per ring pair and
+    rank ("have": recorded once the pair holds the call) serves both
+    directions: the children wait on it before pulling, the parent before
+    refilling the pair with call i + depth; one board channel publishes it.
 
     shape, dtype: one K (or V) tensor. depth: buffer pairs in the ring (2
     lets call i + 1's transfer run during call i's kernel). Construction is
     collective over `group` (an exchange of IPC handles)."""
 
     def __init__(self, shape, dtype=torch.float16, src: int = 0, group=None, depth: int = 2,
-                 device: Optional[torch.device] = None):
+                 device: Optional[torch.device] = None, fanout: Optional[int] = None):
         if depth < 2:
             raise ValueError("depth must be >= 2")
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.src, self.depth, self.group = src, depth, group
         self.is_source = self.rank == src
-        self.receivers: List[int] = [r for r in range(self.world) if r != src]
+        self.fanout = max(1, self.world - 1 if fanout is None else int(fanout))
+        pos = (self.rank - src) % self.world
+        self.parent = None if pos == 0 else (src + (pos - 1) // self.fanout) % self.world
+        self.children: List[int] = [(src + c) % self.world
+                                    for c in range(pos * self.fanout + 1, pos * self.fanout + self.fanout + 1)
+                                    if c < self.world]
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         ring = torch.empty((depth, 2) + tuple(shape), dtype=dtype, device=self.device)
         self.k = [ring[b, 0] for b in range(depth)]
@@ -215,72 +231,75 @@ class KVBroadcast:
         self.calls = 0
         self._sourced = -1
         self.copy_stream = torch.cuda.Stream(self.device)
-        self.board = Board(2, group)  # channels READY (source), PULLED (receivers)
+        self.board = Board(1, group)  # channel HAVE: this rank's ring holds call i
         self._mapped: dict = {}
         self._events: List[_IpcEvent] = []
         with torch.cuda.device(self.device):
-            if self.is_source:
-                self.ready = [self._event() for _ in range(depth)]
-                handle, off = export_tensor(ring)
-                payload = {"ring": (handle, off), "ready": [e.handle for e in self.ready]}
-            else:
-                self.pulled = [self._event() for _ in range(depth)]
+            self.have = [self._event() for _ in range(depth)]
+            if not self.is_source:
                 self.released = [torch.cuda.Event() for _ in range(depth)]
                 self.arrived = [torch.cuda.Event() for _ in range(depth)]
-                payload = {"pulled": [e.handle for e in self.pulled]}
+            handle, off = export_tensor(ring)
+            payload = {"ring": (handle, off), "have": [e.handle for e in self.have]}
             payloads: list = [None] * self.world
             dist.all_gather_object(payloads, payload, group=group)
-            if self.is_source:
-                self.peer_pulled = {r: [self._event(h) for h in payloads[r]["pulled"]] for r in self.receivers}
-            else:
-                handle, off = payloads[src]["ring"]
+            self.child_have = {c: [self._event(h) for h in payloads[c]["have"]] for c in self.children}
+            if self.parent is not None:
+                handle, off = payloads[self.parent]["ring"]
                 if handle not in self._mapped:
                     self._mapped[handle] = open_handle(handle)
                 base = self._mapped[handle] + off
                 pair = 2 * self.nbytes
-                self.src_k = [base + b * pair for b in range(depth)]
-                self.src_v = [base + b * pair + self.nbytes for b in range(depth)]
-                self.src_ready = [self._event(h) for h in payloads[src]["ready"]]
+                self.parent_k = [base + b * pair for b in range(depth)]
+                self.parent_v = [base + b * pair + self.nbytes for b in range(depth)]
+                self.parent_have = [self._event(h) for h in payloads[self.parent]["have"]]
 
     def _event(self, handle: Optional[bytes] = None) -> _IpcEvent:
         e = _IpcEvent(handle)
         self._events.append(e)
         return e
 
+    def _children_done(self, i: int, stream: int) -> None:
+        """`stream` waits until every child has pulled call i - depth out of
+        pair b (so the pair may take call i)."""
+        if i >= self.depth and self.children:
+            b = i % self.depth
+            self.board.wait(_HAVE, self.children, i - self.depth)
+            for c in self.children:
+                self.child_have[c][b].wait_on(stream)
+
     def source(self, i: int) -> Tuple[torch.Tensor, torch.Tensor]:
         """Source rank: the pair to write call i's K and V into, once every
-        receiver has pulled what the pair held before (the current stream
-        waits for that)."""
+        child has pulled what the pair held before (the current stream waits
+        for that)."""
         if not self.is_source:
             raise RuntimeError("source() is for the source rank")
         b = i % self.depth
         self._sourced = i
-        if i >= self.depth and self.receivers:
-            self.board.wait(_PULLED, self.receivers, i - self.depth)
-            cur = torch.cuda.current_stream(self.device).cuda_stream
-            for r in self.receivers:
-                self.peer_pulled[r][b].wait_on(cur)
+        self._children_done(i, torch.cuda.current_stream(self.device).cuda_stream)
         return self.k[b], self.v[b]
 
     def start(self, i: int) -> None:
         """Source: call i's K/V are complete once the current stream reaches
-        this point. Receiver: enqueue the pull of call i's K/V."""
+        this point. Other ranks: enqueue the pull of call i's K/V from the
+        parent."""
         b = i % self.depth
         if self.is_source:
             if self._sourced != i:  # the pair must be free of call i - depth's pulls first
                 self.source(i)
-            self.ready[b].record(torch.cuda.current_stream(self.device).cuda_stream)
-            self.board.publish(_READY, i)
+            self.have[b].record(torch.cuda.current_stream(self.device).cuda_stream)
+            self.board.publish(_HAVE, i)
             return
-        self.board.wait(_READY, [self.src], i)
+        self.board.wait(_HAVE, [self.parent], i)
         cs = self.copy_stream.cuda_stream
-        self.src_ready[b].wait_on(cs)
+        self.parent_have[b].wait_on(cs)
+        self._children_done(i, cs)
         if i >= self.depth:
             self.copy_stream.wait_event(self.released[b])
-        copy_async(self.k[b].data_ptr(), self.src_k[b], self.nbytes, cs)
-        copy_async(self.v[b].data_ptr(), self.src_v[b], self.nbytes, cs)
-        self.pulled[b].record(cs)
-        self.board.publish(_PULLED, i)
+        copy_async(self.k[b].data_ptr(), self.parent_k[b], self.nbytes, cs)
+        copy_async(self.v[b].data_ptr(), self.parent_v[b], self.nbytes, cs)
+        self.have[b].record(cs)
+        self.board.publish(_HAVE, i)
         self.arrived[b].record(self.copy_stream)
 
     def wait(self, i: int) -> Tuple[torch.Tensor, torch.Tensor]:

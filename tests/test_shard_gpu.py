@@ -109,6 +109,16 @@ def _worker(rank, world, port, result_q):
                 errs.append(float((last.float() - full.float()).abs().max()))
         rg.close()
         bc.close()
+        # a chain of pulls (each rank pulls from the previous one; a tree of
+        # fanout 1): on 3+ ranks the non-source parents are exercised
+        bc = KVBroadcast((1, 1, Skv, D), src=0, fanout=1)
+        outs = [torch.full((1, 1, Sq, D), float("nan"), dtype=torch.float16, device="cuda") for _ in ins]
+        for _ in range(2):  # call indices run on across uses
+            shard.attention_by_rows_copy_engine([c[0] for c in calls], bc, D ** -0.5, Sq, outs, fill=fill)
+        for (q, k, v), out in zip(ins, outs):
+            full = gfx906_b200.attn(q.cuda(), k.cuda(), v.cuda(), D ** -0.5)
+            errs.append(float((out.float() - full.float()).abs().max()))
+        bc.close()
         torch.cuda.synchronize()
         if rank == 0:
             result_q.put(errs)
@@ -125,4 +135,4 @@ def test_sharded_attention_nccl():
     q = ctx.Queue()
     mp.start_processes(_worker, args=(world, _free_port(), q), nprocs=world, start_method="spawn", join=True)
     errs = q.get(timeout=120)
-    assert all(e <= 2e-3 for e in errs) and len(errs) == 13, errs
+    assert all(e <= 2e-3 for e in errs) and len(errs) == 16, errs
